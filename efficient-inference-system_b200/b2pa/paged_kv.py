@@ -1,0 +1,340 @@
+"""Paged KV cache: per-layer block pool, per-request block tables, batched view.
+
+Host-side mirror of the reference's ``src/cache/paged_kv.py``
+(jacobzhang22/efficient-inference-system).  Class names, attributes, the
+allocation order and the return values are the reference's, so code written
+against ``LayerBlockPool`` / ``PagedKVCacheState`` / ``BatchedPagedKVCache``
+runs unchanged.  What differs is where the bytes move:
+
+* block allocation stays on the host, exactly as in the reference
+  (LIFO free list, geometric growth by ``torch.cat``; paged_kv.py:44-85);
+* the K/V copies of a whole ``append_batch`` call are one launch of the
+  ``b2pa_kv_append`` scatter kernel instead of two slice copies per touched
+  block per request (paged_kv.py:109-120, 165-171);
+* releasing a request zeroes all of its blocks with one ``b2pa_zero_blocks``
+  launch instead of two ``zero_()`` calls per block (paged_kv.py:80-85).
+
+Pools live on a CUDA device.  Pools on the ``meta`` device are accepted for
+host-only bookkeeping (allocation order, page tables) with no data movement;
+CPU pools are rejected -- there is no CPU path in this package.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import _lib
+from ._staging import stage_int32
+
+
+class LayerBlockPool:
+    """Block pool of one layer: K and V tensors ``[blocks, H, block_size, D]``.
+
+    Mirrors ``LayerBlockPool`` (src/cache/paged_kv.py:9-93).
+    """
+
+    def __init__(self, block_size: int, initial_blocks: int, growth_factor: float):
+        self.block_size = block_size
+        self.initial_blocks = initial_blocks
+        self.growth_factor = growth_factor
+        self.k_blocks: torch.Tensor | None = None
+        self.v_blocks: torch.Tensor | None = None
+        self.num_heads: int | None = None
+        self.head_dim: int | None = None
+        self.dtype: torch.dtype | None = None
+        self.device: torch.device | None = None
+        self.free_block_ids: list[int] = []
+        self.capacity_blocks = 0
+
+    def ensure_initialized(self, num_heads: int, head_dim: int, dtype: torch.dtype, device: torch.device) -> None:
+        """Lazily allocates the pool on first use (paged_kv.py:28-42)."""
+        if self.k_blocks is not None:
+            return
+        device = torch.device(device)
+        if device.type not in ("cuda", "meta"):
+            raise RuntimeError(f"b2pa pools live on CUDA devices (or 'meta' for bookkeeping), not {device}")
+        self.num_heads = num_heads
+        self.head_dim = head_dim
+        self.dtype = dtype
+        self.device = device
+        self._grow(self.initial_blocks)
+
+    def _grow(self, min_extra_blocks: int) -> None:
+        """Geometric growth, same arithmetic as paged_kv.py:44-73."""
+        if self.num_heads is None or self.head_dim is None or self.dtype is None or self.device is None:
+            raise ValueError("Pool must be initialized before growth.")
+        grow_by = max(
+            min_extra_blocks,
+            self.initial_blocks if self.capacity_blocks == 0
+            else int(math.ceil(self.capacity_blocks * (self.growth_factor - 1.0))),
+        )
+        grow_by = max(grow_by, 1)
+        new_k = torch.zeros(grow_by, self.num_heads, self.block_size, self.head_dim, dtype=self.dtype,
+                            device=self.device)
+        new_v = torch.zeros_like(new_k)
+        if self.k_blocks is None:
+            self.k_blocks = new_k
+            self.v_blocks = new_v
+        else:
+            self.k_blocks = torch.cat([self.k_blocks, new_k], dim=0)
+            self.v_blocks = torch.cat([self.v_blocks, new_v], dim=0)
+        start = self.capacity_blocks
+        self.capacity_blocks += grow_by
+        self.free_block_ids.extend(range(start, self.capacity_blocks))
+
+    def allocate_block(self) -> int:
+        """LIFO pop, growing by at least one block when empty (paged_kv.py:75-78)."""
+        if not self.free_block_ids:
+            self._grow(1)
+        return self.free_block_ids.pop()
+
+    def release_block(self, block_id: int) -> None:
+        """Zeroes one block and returns it to the free list (paged_kv.py:80-85)."""
+        self.release_blocks([block_id])
+
+    def release_blocks(self, block_ids: list[int]) -> None:
+        """Zeroes ``block_ids`` in one kernel launch, then frees them in order."""
+        if self.k_blocks is None or self.v_blocks is None:
+            return
+        if block_ids and self.k_blocks.device.type == "cuda":
+            _zero_blocks(self, block_ids)
+        self.free_block_ids.extend(block_ids)
+
+    def bytes_per_block(self) -> int:
+        if self.k_blocks is None:
+            return 0
+        return 2 * self.k_blocks[0].numel() * self.k_blocks.element_size()
+
+    def reserved_bytes(self) -> int:
+        return self.capacity_blocks * self.bytes_per_block()
+
+
+@dataclass
+class PagedKVCacheState:
+    """Block table and length of one request in one layer (paged_kv.py:96-137)."""
+
+    pool: LayerBlockPool
+    block_ids: list[int] = field(default_factory=list)
+    seq_len: int = 0
+
+    def reserve(self, length: int) -> int:
+        """Allocates the blocks ``length`` more tokens need and advances
+        ``seq_len``; returns the position of the first new token."""
+        return reserve_tokens(self, length)
+
+    def append(self, k_new: torch.Tensor, v_new: torch.Tensor, length: int) -> None:
+        """Appends the first ``length`` tokens of ``k_new[0]``/``v_new[0]``."""
+        if length <= 0:
+            return
+        BatchedPagedKVCache([self], pool=self.pool).append_batch(k_new[:1], v_new[:1], [length])
+
+    def release(self) -> None:
+        self.pool.release_blocks(list(self.block_ids))
+        self.block_ids.clear()
+        self.seq_len = 0
+
+    def live_bytes(self) -> int:
+        if self.pool.k_blocks is None:
+            return 0
+        kb = self.pool.k_blocks
+        return self.seq_len * kb.shape[1] * kb.shape[3] * 2 * kb.element_size()
+
+    def reserved_bytes(self) -> int:
+        return len(self.block_ids) * self.pool.bytes_per_block()
+
+    def fragmentation_bytes(self) -> int:
+        return self.reserved_bytes() - self.live_bytes()
+
+
+def host_lengths(current_lengths, T: int, B: int) -> list[int]:
+    """Per-request token counts as append_batch reads them (paged_kv.py:157-162)."""
+    if current_lengths is None:
+        return [T] * B
+    if isinstance(current_lengths, int):
+        return [current_lengths] * B
+    if isinstance(current_lengths, torch.Tensor):
+        return [int(x) for x in current_lengths.tolist()]
+    return [int(x) for x in current_lengths]
+
+
+class BatchedPagedKVCache:
+    """The requests of one layer seen as a batch (paged_kv.py:140-206)."""
+
+    def __init__(self, states: list[PagedKVCacheState], pool: LayerBlockPool | None = None):
+        self.states = states
+        if pool is not None:
+            self.pool = pool
+        else:
+            non_null = next((state for state in states if state is not None), None)
+            if non_null is None:
+                raise ValueError("BatchedPagedKVCache needs a pool when all states are uninitialized.")
+            self.pool = non_null.pool
+
+    def plan_append(self, k_new: torch.Tensor, lengths: list[int]) -> list[int]:
+        """Host half of ``append_batch``: initialises the pool and allocates
+        blocks request by request; returns each request's start position."""
+        return plan_append(self, k_new, lengths)
+
+    def append_batch(self, k_new: torch.Tensor, v_new: torch.Tensor,
+                     current_lengths: int | torch.Tensor | list[int] | None = None) -> torch.Tensor:
+        """Writes each request's new tokens into its blocks; returns the new
+        sequence lengths as int64 (paged_kv.py:151-172)."""
+        return append_batch_into(self, k_new, v_new, current_lengths)
+
+    def page_table_array(self) -> np.ndarray:
+        """int32 ``[B, max_pages]`` block table, -1 padded (paged_kv.py:174-193)."""
+        max_pages = max((len(s.block_ids) for s in self.states), default=0)
+        table = np.full((len(self.states), max_pages), -1, dtype=np.int32)
+        for row, s in enumerate(self.states):
+            if s.block_ids:
+                table[row, : len(s.block_ids)] = s.block_ids
+        return table
+
+    def page_table_tensor(self, device: torch.device | None = None) -> torch.Tensor:
+        device = device or self.pool.device
+        return torch.from_numpy(self.page_table_array()).to(device)
+
+    def seq_lens_tensor(self, device: torch.device | None = None) -> torch.Tensor:
+        device = device or self.pool.device
+        return torch.tensor([s.seq_len for s in self.states], dtype=torch.int32, device=device)
+
+    def live_bytes(self) -> int:
+        return sum(s.live_bytes() for s in self.states)
+
+    def reserved_bytes(self) -> int:
+        return sum(s.reserved_bytes() for s in self.states)
+
+    def fragmentation_bytes(self) -> int:
+        return sum(s.fragmentation_bytes() for s in self.states)
+
+
+# ------------------------------------------------- duck-typed host logic
+# These functions read and write only the attributes the reference's own
+# classes have (states, pool, block_ids, seq_len, allocate_block,
+# ensure_initialized, block_size), so they serve both this module's classes
+# and the reference's when the backend is installed into it.
+
+def reserve_tokens(state, length: int) -> int:
+    """Allocates blocks for ``length`` more tokens of ``state`` in the
+    reference's order -- one block each time the write position reaches a
+    block boundary (paged_kv.py:110-113) -- advances ``seq_len`` and returns
+    the position of the first new token.  The pool must be initialised."""
+    start = state.seq_len
+    if length <= 0:
+        return start
+    bs = state.pool.block_size
+    need = -(-(start + length) // bs) - (-(-start // bs))
+    for _ in range(need):
+        state.block_ids.append(state.pool.allocate_block())
+    state.seq_len = start + length
+    return start
+
+
+def plan_append(cache, k_new: torch.Tensor, lengths: list[int]) -> list[int]:
+    """Initialises the pool and allocates blocks request by request, in batch
+    order (paged_kv.py:165-171); returns each request's start position."""
+    _, H, T, D = k_new.shape
+    starts = []
+    for b, state in enumerate(cache.states):
+        if state.pool is not cache.pool:
+            raise ValueError("b2pa: all states of a BatchedPagedKVCache must share its pool")
+        n = max(min(lengths[b], T), 0)
+        if n > 0:
+            state.pool.ensure_initialized(H, D, k_new.dtype, k_new.device)
+        starts.append(reserve_tokens(state, n))
+    return starts
+
+
+def append_batch_into(cache, k_new: torch.Tensor, v_new: torch.Tensor, current_lengths=None) -> torch.Tensor:
+    """``BatchedPagedKVCache.append_batch`` (paged_kv.py:151-172): host block
+    allocation, then one scatter-kernel launch for every copied token."""
+    B, H, T, D = k_new.shape
+    if B != len(cache.states):
+        raise ValueError(f"k_new has {B} rows for {len(cache.states)} states")
+    if v_new.shape != k_new.shape or v_new.dtype != k_new.dtype:
+        raise ValueError("k_new and v_new must have the same shape and dtype")
+    lengths = host_lengths(current_lengths, T, B)
+    clamped = [max(min(n, T), 0) for n in lengths]
+    if any(clamped) and k_new.device.type not in ("cuda", "meta"):
+        raise RuntimeError("b2pa: k_new must be a CUDA tensor (this package has no CPU path)")
+    starts = plan_append(cache, k_new, clamped)
+    if any(clamped) and k_new.device.type == "cuda":
+        _kv_append(cache, k_new, v_new, starts, clamped)
+    return torch.tensor([s.seq_len for s in cache.states], dtype=torch.long, device=k_new.device)
+
+
+# ----------------------------------------------------------------- launches
+def _require_cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise RuntimeError(f"b2pa: {what} must be a CUDA tensor (this package has no CPU path)")
+
+
+def device_metadata(cache, device: torch.device, extra: list[list[int]] | None = None):
+    """Uploads the block table and sequence lengths of ``cache`` (plus any
+    ``extra`` int32 rows) with one pinned host->device copy.
+
+    Returns ``(page_table[B, max_pages], seq_lens[B], extras..., max_pages)``
+    as int32 device tensors.  Works on the reference's own cache objects as
+    well as on this module's: only ``states[i].block_ids`` / ``seq_len`` are
+    read.
+    """
+    states = cache.states
+    B = len(states)
+    max_pages = max((len(s.block_ids) for s in states), default=0)
+    rows = 1 + (len(extra) if extra else 0)
+    n = B * max_pages + B * rows
+    host = np.empty(n, dtype=np.int32)
+    if max_pages:
+        table = host[: B * max_pages].reshape(B, max_pages)
+        table.fill(-1)
+        for r, s in enumerate(states):
+            ids = s.block_ids
+            if ids:
+                table[r, : len(ids)] = ids
+    o = B * max_pages
+    host[o:o + B] = [s.seq_len for s in states]
+    if extra:
+        for i, row in enumerate(extra):
+            host[o + B * (i + 1): o + B * (i + 2)] = row
+    dev = stage_int32(host, device)
+    page_table = dev[: B * max_pages].view(B, max_pages)
+    outs = [page_table]
+    for i in range(rows):
+        outs.append(dev[o + B * i: o + B * (i + 1)])
+    outs.append(max_pages)
+    return tuple(outs)
+
+
+def _kv_append(cache, k_new: torch.Tensor, v_new: torch.Tensor, starts: list[int], lengths: list[int]) -> None:
+    _require_cuda(k_new, "k_new")
+    _require_cuda(v_new, "v_new")
+    pool = cache.pool
+    kb, vb = pool.k_blocks, pool.v_blocks
+    if kb.device != k_new.device:
+        raise ValueError(f"pool on {kb.device} but k_new on {k_new.device}")
+    B, H, T, D = k_new.shape
+    dev = k_new.device
+    page_table, _seq, start_t, len_t, max_pages = device_metadata(cache, dev, [starts, lengths])
+    lib = _lib.load()
+    rc = lib.b2pa_kv_append(
+        k_new.data_ptr(), _lib.strides4(k_new), v_new.data_ptr(), _lib.strides4(v_new),
+        kb.data_ptr(), vb.data_ptr(), _lib.strides4(kb), kb.shape[0],
+        page_table.data_ptr() if max_pages else None, max(max_pages, 1), max_pages,
+        start_t.data_ptr(), len_t.data_ptr(), B, H, T, D, pool.block_size, _lib.dtype_code(k_new.dtype),
+        _lib.status_buffer(dev).data_ptr(), _lib.stream_handle(dev))
+    _lib.check(rc, "b2pa_kv_append")
+
+
+def _zero_blocks(pool: LayerBlockPool, block_ids: list[int]) -> None:
+    kb, vb = pool.k_blocks, pool.v_blocks
+    dev = kb.device
+    ids = stage_int32(np.asarray(block_ids, dtype=np.int32), dev)
+    lib = _lib.load()
+    rc = lib.b2pa_zero_blocks(kb.data_ptr(), vb.data_ptr(), _lib.strides4(kb), kb.shape[0], ids.data_ptr(),
+                              len(block_ids), kb.shape[1], kb.shape[3], kb.shape[2], _lib.dtype_code(kb.dtype),
+                              _lib.status_buffer(dev).data_ptr(), _lib.stream_handle(dev))
+    _lib.check(rc, "b2pa_zero_blocks")

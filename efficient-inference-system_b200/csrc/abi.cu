@@ -1,0 +1,354 @@
+// abi.cu -- extern "C" entry points of libb2pa.so (declared in b2pa.h).
+//
+// Each entry point validates its arguments on the host, maps them onto the
+// launcher structs of kernels.h and enqueues the kernels on the caller's
+// stream.  Nothing here allocates device memory or synchronises, except the
+// explicit b2pa_status_read().  Errors come back as b2pa_status codes with a
+// thread-local message; no C++ exception crosses the ABI.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <tuple>
+
+#include "b2pa.h"
+#include "kernels.h"
+
+namespace b2pa {
+
+static thread_local std::string g_last_error;
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+static int current_device() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  return dev;
+}
+
+static constexpr int kMaxDevices = 64;
+
+int device_sm_count() {
+  static int cache[kMaxDevices] = {0};
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = n > 0 ? n : 148;
+  }
+  return cache[dev];
+}
+
+int device_max_smem_optin() {
+  static int cache[kMaxDevices] = {0};
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return 227 * 1024;
+  if (cache[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cache[dev] = n > 0 ? n : 227 * 1024;
+  }
+  return cache[dev];
+}
+
+int decode_occupancy_cached(const void* func, int threads, size_t smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, size_t, int>, int> cache;
+  const auto key = std::make_tuple(func, threads, smem, current_device());
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, func, threads, smem) != cudaSuccess) n = 0;
+  std::lock_guard<std::mutex> g(mu);
+  cache[key] = n;
+  return n;
+}
+
+// Split size: enough work items to keep every resident CTA busy with a
+// balanced share (about 2048 items for a 148-SM part at 2 CTAs per SM),
+// pages per split kept between 4 and 64.
+static int choose_pages_per_split(int B, int HG, int max_pages) {
+  const int64_t target_items = 2048;
+  const int64_t pairs = (int64_t)B * HG;
+  int64_t splits = pairs > 0 ? (target_items + pairs - 1) / pairs : 1;
+  if (splits < 1) splits = 1;
+  int64_t P = (max_pages + splits - 1) / splits;
+  if (P < 4) P = 4;
+  if (P > 64) P = 64;
+  return (int)P;
+}
+
+static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+DecodePlan make_decode_plan(int B, int H, int D, int max_pages, int block_size, int dtype) {
+  DecodePlan pl;
+  const int hpb = block_size * D * dtype_size(dtype);
+  int G = 1;
+  for (int g : {4, 2}) {
+    if (H % g == 0 && 2 * g * hpb <= 48 * 1024) {
+      G = g;
+      break;
+    }
+  }
+  pl.G = G;
+  pl.HG = H / G;
+  pl.pages_per_split = choose_pages_per_split(B, pl.HG, max_pages);
+  const int64_t splits = max_pages > 0 ? (max_pages + pl.pages_per_split - 1) / pl.pages_per_split : 1;
+  pl.max_items = (int64_t)B * pl.HG * (splits > 0 ? splits : 1);
+  size_t off = 0;
+  pl.off_item_off = off;
+  off = align_up(off + 4ull * (B + 1), 256);
+  pl.off_part_ml = off;
+  off = align_up(off + 8ull * pl.max_items * G, 256);
+  pl.off_part_acc = off;
+  off = align_up(off + 4ull * pl.max_items * G * D, 256);
+  pl.bytes = off;
+  return pl;
+}
+
+}  // namespace b2pa
+
+using namespace b2pa;
+
+namespace {
+
+bool aligned_to(const void* p, size_t a) { return reinterpret_cast<uintptr_t>(p) % a == 0; }
+
+// Shared validation of the attention entry points.  Returns B2PA_OK or an
+// error code with the message set.
+int validate_attention(const char* fn, const void* q, const int64_t* qs, const void* k_pool, const void* v_pool,
+                       const int64_t* ps, int64_t num_blocks, const int32_t* page_table, int64_t pt_stride,
+                       int max_pages, const int32_t* seq_lens, const int32_t* cur_lens, void* out,
+                       const int64_t* os, int B, int H, int T, int D, int block_size, int dtype) {
+  if (B < 0 || H <= 0 || T < 0 || D <= 0 || block_size <= 0 || max_pages < 0 || num_blocks < 0)
+    return set_error(B2PA_ERR_INVALID_ARGUMENT, "%s: bad sizes B=%d H=%d T=%d D=%d block_size=%d max_pages=%d", fn, B,
+                     H, T, D, block_size, max_pages);
+  if (dtype_size(dtype) == 0) return set_error(B2PA_ERR_UNSUPPORTED, "%s: unknown dtype %d", fn, dtype);
+  if (!head_dim_supported(D)) return set_error(B2PA_ERR_UNSUPPORTED, "%s: head_dim %d not built", fn, D);
+  if (!block_size_supported(block_size))
+    return set_error(B2PA_ERR_UNSUPPORTED, "%s: block_size %d not built", fn, block_size);
+  if (B == 0 || T == 0) return B2PA_OK;
+  if (!q || !k_pool || !v_pool || !seq_lens || !cur_lens || !out || !qs || !ps || !os)
+    return set_error(B2PA_ERR_INVALID_ARGUMENT, "%s: null pointer argument", fn);
+  if (max_pages > 0 && !page_table) return set_error(B2PA_ERR_INVALID_ARGUMENT, "%s: null page_table", fn);
+  if (max_pages > 0 && pt_stride < max_pages)
+    return set_error(B2PA_ERR_INVALID_ARGUMENT, "%s: page-table row stride %lld < max_pages %d", fn,
+                     (long long)pt_stride, max_pages);
+  const int64_t es = dtype_size(dtype);
+  if (ps[3] != 1 || ps[2] != D || ps[1] != (int64_t)block_size * D || ps[0] != (int64_t)H * block_size * D)
+    return set_error(B2PA_ERR_UNSUPPORTED, "%s: pools must be contiguous [num_blocks, H, block_size, D]", fn);
+  if (!aligned_to(k_pool, 16) || !aligned_to(v_pool, 16))
+    return set_error(B2PA_ERR_UNSUPPORTED, "%s: pool base pointers must be 16-byte aligned", fn);
+  if (qs[3] != 1 || os[3] != 1) return set_error(B2PA_ERR_UNSUPPORTED, "%s: q/out need a unit D stride", fn);
+  // Rows of q and out are moved as 16-byte words (or narrower for D*es < 16).
+  const int64_t row_align = (D * es) >= 16 ? 16 : D * es;
+  if (!aligned_to(q, row_align) || !aligned_to(out, row_align))
+    return set_error(B2PA_ERR_UNSUPPORTED, "%s: q/out must be %lld-byte aligned", fn, (long long)row_align);
+  for (int i = 0; i < 3; ++i)
+    if ((qs[i] * es) % row_align || (os[i] * es) % row_align)
+      return set_error(B2PA_ERR_UNSUPPORTED, "%s: q/out strides must keep rows %lld-byte aligned", fn,
+                       (long long)row_align);
+  return B2PA_OK;
+}
+
+AttnArgs make_attn_args(const void* q, const int64_t* qs, const void* k_pool, const void* v_pool, int64_t num_blocks,
+                        const int32_t* page_table, int64_t pt_stride, int max_pages, const int32_t* seq_lens,
+                        const int32_t* cur_lens, void* out, const int64_t* os, int B, int H, int T, int D,
+                        int block_size, float scale, int dtype, void* workspace, size_t workspace_bytes,
+                        int32_t* status) {
+  AttnArgs a;
+  a.q = q;
+  for (int i = 0; i < 4; ++i) {
+    a.sq[i] = qs[i];
+    a.so[i] = os[i];
+  }
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.num_blocks = num_blocks;
+  a.page_table = page_table;
+  a.pt_stride = pt_stride;
+  a.max_pages = max_pages;
+  a.seq_lens = seq_lens;
+  a.cur_lens = cur_lens;
+  a.out = out;
+  a.B = B;
+  a.H = H;
+  a.T = T;
+  a.D = D;
+  a.block_size = block_size;
+  a.dtype = dtype;
+  a.scale = scale;
+  a.workspace = workspace;
+  a.workspace_bytes = workspace_bytes;
+  a.status = status;
+  return a;
+}
+
+}  // namespace
+
+extern "C" {
+
+int b2pa_abi_version(void) { return B2PA_ABI_VERSION; }
+
+const char* b2pa_last_error_string(void) { return g_last_error.c_str(); }
+
+int b2pa_status_read(const int32_t* status, int32_t* host_status, void* stream) {
+  if (!status || !host_status) return set_error(B2PA_ERR_INVALID_ARGUMENT, "status_read: null pointer");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaMemcpyAsync(host_status, status, sizeof(int32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "status_read: %s", cudaGetErrorString(e));
+  return B2PA_OK;
+}
+
+int b2pa_status_clear(int32_t* status, void* stream) {
+  if (!status) return set_error(B2PA_ERR_INVALID_ARGUMENT, "status_clear: null pointer");
+  cudaError_t e = cudaMemsetAsync(status, 0, sizeof(int32_t), static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "status_clear: %s", cudaGetErrorString(e));
+  return B2PA_OK;
+}
+
+int b2pa_kv_append(const void* k_new, const int64_t new_k_strides[4], const void* v_new,
+                   const int64_t new_v_strides[4], void* k_pool, void* v_pool, const int64_t pool_strides[4],
+                   int64_t num_blocks, const int32_t* page_table, int64_t pt_stride, int max_pages,
+                   const int32_t* start_pos, const int32_t* lengths, int B, int H, int T, int D, int block_size,
+                   int dtype, int32_t* status, void* stream) {
+  if (B < 0 || H <= 0 || T < 0 || D <= 0 || block_size <= 0 || max_pages < 0 || num_blocks < 0)
+    return set_error(B2PA_ERR_INVALID_ARGUMENT, "kv_append: bad sizes B=%d H=%d T=%d D=%d block_size=%d", B, H, T, D,
+                     block_size);
+  if (dtype_size(dtype) == 0) return set_error(B2PA_ERR_UNSUPPORTED, "kv_append: unknown dtype %d", dtype);
+  if (B == 0 || T == 0) return B2PA_OK;
+  if (!k_new || !v_new || !k_pool || !v_pool || !new_k_strides || !new_v_strides || !pool_strides || !start_pos ||
+      !lengths)
+    return set_error(B2PA_ERR_INVALID_ARGUMENT, "kv_append: null pointer argument");
+  if (max_pages > 0 && (!page_table || pt_stride < max_pages))
+    return set_error(B2PA_ERR_INVALID_ARGUMENT, "kv_append: bad page table");
+  const int64_t* ps = pool_strides;
+  if (ps[3] != 1 || ps[2] != D || ps[1] != (int64_t)block_size * D || ps[0] != (int64_t)H * block_size * D)
+    return set_error(B2PA_ERR_UNSUPPORTED, "kv_append: pools must be contiguous [num_blocks, H, block_size, D]");
+  AppendArgs a;
+  a.k_new = k_new;
+  a.v_new = v_new;
+  for (int i = 0; i < 4; ++i) {
+    a.sk[i] = new_k_strides[i];
+    a.sv[i] = new_v_strides[i];
+  }
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.num_blocks = num_blocks;
+  a.page_table = page_table;
+  a.pt_stride = pt_stride;
+  a.max_pages = max_pages;
+  a.start_pos = start_pos;
+  a.lengths = lengths;
+  a.B = B;
+  a.H = H;
+  a.T = T;
+  a.D = D;
+  a.block_size = block_size;
+  a.dtype = dtype;
+  a.status = status;
+  return launch_kv_append(a, static_cast<cudaStream_t>(stream));
+}
+
+size_t b2pa_paged_decode_workspace_size(int B, int H, int D, int max_pages, int block_size, int dtype) {
+  if (B <= 0 || H <= 0 || D <= 0 || max_pages < 0 || block_size <= 0 || dtype_size(dtype) == 0) return 0;
+  return make_decode_plan(B, H, D, max_pages, block_size, dtype).bytes;
+}
+
+int b2pa_paged_decode(const void* q, const int64_t q_strides[4], const void* k_pool, const void* v_pool,
+                      const int64_t pool_strides[4], int64_t num_blocks, const int32_t* page_table,
+                      int64_t pt_stride, int max_pages, const int32_t* seq_lens, const int32_t* cur_lens, void* out,
+                      const int64_t out_strides[4], int B, int H, int D, int block_size, float scale, int dtype,
+                      void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  int rc = validate_attention("paged_decode", q, q_strides, k_pool, v_pool, pool_strides, num_blocks, page_table,
+                              pt_stride, max_pages, seq_lens, cur_lens, out, out_strides, B, H, 1, D, block_size,
+                              dtype);
+  if (rc != B2PA_OK || B == 0) return rc;
+  const DecodePlan plan = make_decode_plan(B, H, D, max_pages, block_size, dtype);
+  if (!workspace || workspace_bytes < plan.bytes)
+    return set_error(B2PA_ERR_WORKSPACE, "paged_decode: workspace of %zu bytes, %zu needed", workspace_bytes,
+                     plan.bytes);
+  if (!aligned_to(workspace, 256)) return set_error(B2PA_ERR_WORKSPACE, "paged_decode: workspace must be 256-byte aligned");
+  if (plan.max_items > INT32_MAX)
+    return set_error(B2PA_ERR_UNSUPPORTED, "paged_decode: %lld work items exceed the int32 plan", (long long)plan.max_items);
+  AttnArgs a = make_attn_args(q, q_strides, k_pool, v_pool, num_blocks, page_table, pt_stride, max_pages, seq_lens,
+                              cur_lens, out, out_strides, B, H, 1, D, block_size, scale, dtype, workspace,
+                              workspace_bytes, status);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case B2PA_DTYPE_F32: return launch_paged_decode_f32(a, plan, s);
+    case B2PA_DTYPE_BF16: return launch_paged_decode_bf16(a, plan, s);
+    default: return launch_paged_decode_f16(a, plan, s);
+  }
+}
+
+size_t b2pa_paged_prefill_workspace_size(int B, int H, int T, int D, int max_pages, int block_size, int dtype) {
+  (void)B; (void)H; (void)T; (void)D; (void)max_pages; (void)block_size; (void)dtype;
+  return 0;
+}
+
+int b2pa_paged_prefill(const void* q, const int64_t q_strides[4], const void* k_pool, const void* v_pool,
+                       const int64_t pool_strides[4], int64_t num_blocks, const int32_t* page_table,
+                       int64_t pt_stride, int max_pages, const int32_t* seq_lens, const int32_t* cur_lens, void* out,
+                       const int64_t out_strides[4], int B, int H, int T, int D, int block_size, float scale,
+                       int dtype, void* workspace, size_t workspace_bytes, int32_t* status, void* stream) {
+  int rc = validate_attention("paged_prefill", q, q_strides, k_pool, v_pool, pool_strides, num_blocks, page_table,
+                              pt_stride, max_pages, seq_lens, cur_lens, out, out_strides, B, H, T, D, block_size,
+                              dtype);
+  if (rc != B2PA_OK || B == 0 || T == 0) return rc;
+  if (T > 65535 * 32) return set_error(B2PA_ERR_UNSUPPORTED, "paged_prefill: T=%d too large", T);
+  AttnArgs a = make_attn_args(q, q_strides, k_pool, v_pool, num_blocks, page_table, pt_stride, max_pages, seq_lens,
+                              cur_lens, out, out_strides, B, H, T, D, block_size, scale, dtype, workspace,
+                              workspace_bytes, status);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case B2PA_DTYPE_F32: return launch_paged_prefill_f32(a, s);
+    case B2PA_DTYPE_BF16: return launch_paged_prefill_bf16(a, s);
+    default: return launch_paged_prefill_f16(a, s);
+  }
+}
+
+int b2pa_zero_blocks(void* k_pool, void* v_pool, const int64_t pool_strides[4], int64_t num_blocks,
+                     const int32_t* block_ids, int n_ids, int H, int D, int block_size, int dtype, int32_t* status,
+                     void* stream) {
+  if (n_ids < 0 || H <= 0 || D <= 0 || block_size <= 0 || num_blocks < 0)
+    return set_error(B2PA_ERR_INVALID_ARGUMENT, "zero_blocks: bad sizes");
+  if (dtype_size(dtype) == 0) return set_error(B2PA_ERR_UNSUPPORTED, "zero_blocks: unknown dtype %d", dtype);
+  if (n_ids == 0) return B2PA_OK;
+  if (!k_pool || !v_pool || !block_ids || !pool_strides)
+    return set_error(B2PA_ERR_INVALID_ARGUMENT, "zero_blocks: null pointer argument");
+  const int64_t* ps = pool_strides;
+  if (ps[3] != 1 || ps[2] != D || ps[1] != (int64_t)block_size * D || ps[0] != (int64_t)H * block_size * D)
+    return set_error(B2PA_ERR_UNSUPPORTED, "zero_blocks: pools must be contiguous");
+  ZeroArgs a;
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.num_blocks = num_blocks;
+  a.block_ids = block_ids;
+  a.n_ids = n_ids;
+  a.H = H;
+  a.D = D;
+  a.block_size = block_size;
+  a.dtype = dtype;
+  a.status = status;
+  return launch_zero_blocks(a, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

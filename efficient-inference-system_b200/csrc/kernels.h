@@ -1,0 +1,100 @@
+// kernels.h -- host-side launcher interface between the C ABI (abi.cu) and
+// the kernel translation units.  Arguments are validated by abi.cu before a
+// launcher runs; launchers return a b2pa_status and record details through
+// set_error().
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "b2pa.h"
+
+namespace b2pa {
+
+// Records a formatted error message for b2pa_last_error_string() and returns
+// `code` so callers can `return set_error(code, ...)`.
+int set_error(int code, const char* fmt, ...);
+
+// Multiprocessor count of the current device (cached per device).
+int device_sm_count();
+
+// Largest dynamic shared memory per block on the current device (opt-in).
+int device_max_smem_optin();
+
+struct AppendArgs {
+  const void* k_new;
+  const void* v_new;
+  int64_t sk[4];  // k_new element strides [B,H,T,D]
+  int64_t sv[4];  // v_new element strides
+  void* k_pool;
+  void* v_pool;
+  int64_t num_blocks;
+  const int32_t* page_table;
+  int64_t pt_stride;
+  int max_pages;
+  const int32_t* start_pos;
+  const int32_t* lengths;
+  int B, H, T, D, block_size, dtype;
+  int32_t* status;
+};
+
+struct ZeroArgs {
+  void* k_pool;
+  void* v_pool;
+  int64_t num_blocks;
+  const int32_t* block_ids;
+  int n_ids;
+  int H, D, block_size, dtype;
+  int32_t* status;
+};
+
+struct AttnArgs {
+  const void* q;
+  int64_t sq[4];  // q element strides [B,H,T,D]
+  const void* k_pool;
+  const void* v_pool;
+  int64_t num_blocks;
+  const int32_t* page_table;
+  int64_t pt_stride;
+  int max_pages;
+  const int32_t* seq_lens;
+  const int32_t* cur_lens;
+  void* out;
+  int64_t so[4];  // out element strides
+  int B, H, T, D, block_size, dtype;
+  float scale;
+  void* workspace;
+  size_t workspace_bytes;
+  int32_t* status;
+};
+
+int launch_kv_append(const AppendArgs& a, cudaStream_t stream);
+int launch_zero_blocks(const ZeroArgs& a, cudaStream_t stream);
+
+// Decode planning shared by the workspace query and the launcher.
+struct DecodePlan {
+  int G;                // heads per CTA (consumer warps)
+  int HG;               // head groups = H / G
+  int pages_per_split;  // P
+  int64_t max_items;    // upper bound on work items
+  size_t off_item_off, off_part_ml, off_part_acc, bytes;
+};
+DecodePlan make_decode_plan(int B, int H, int D, int max_pages, int block_size, int dtype);
+
+int launch_paged_decode_f32(const AttnArgs& a, const DecodePlan& plan, cudaStream_t s);
+int launch_paged_decode_bf16(const AttnArgs& a, const DecodePlan& plan, cudaStream_t s);
+int launch_paged_decode_f16(const AttnArgs& a, const DecodePlan& plan, cudaStream_t s);
+
+int launch_paged_prefill_f32(const AttnArgs& a, cudaStream_t s);
+int launch_paged_prefill_bf16(const AttnArgs& a, cudaStream_t s);
+int launch_paged_prefill_f16(const AttnArgs& a, cudaStream_t s);
+
+inline int dtype_size(int dtype) {
+  return dtype == B2PA_DTYPE_F32 ? 4 : (dtype == B2PA_DTYPE_BF16 || dtype == B2PA_DTYPE_F16) ? 2 : 0;
+}
+
+inline bool head_dim_supported(int D) { return D == 16 || D == 32 || D == 64 || D == 128 || D == 256; }
+inline bool block_size_supported(int bs) { return bs == 8 || bs == 16 || bs == 32; }
+
+}  // namespace b2pa

@@ -1,0 +1,576 @@
+// paged_decode.cuh -- single-query paged decode attention for sm_100a.
+//
+// Replaces the Triton decode kernel of the reference
+// (src/kernels/triton_paged_attention.py:10-85, launcher :179-217), which
+// runs one program per (sequence, head) and walks every token of the page
+// table sequentially.  Semantics follow the torch reference
+// (src/kernels/reference_paged_attention.py:31-57): for sequence b the query
+// sits at position seq_len - cur_len and sees keys
+// 0 .. min(seq_len, seq_len - cur_len + 1) - 1; out = softmax(q.K^T * scale).V
+// in fp32, zeros when no key is visible, stored in the element type.
+//
+// Design (HBM-bound gather, no tensor cores):
+//   * work item = (sequence b, head group of G heads, split of P pages).
+//     A one-CTA plan kernel turns seq_lens/cur_lens into per-sequence item
+//     offsets; a persistent grid (SMs x resident CTAs) strides over items.
+//   * per CTA: one producer warp + G consumer warps.  The producer walks the
+//     block table and moves, per page, the G contiguous [block_size, D] head
+//     pages of K and of V with two cp.async.bulk copies into a ring of
+//     shared-memory stages guarded by full/empty mbarriers (no multicast).
+//     It also stages the pre-scaled query of the item and a small metadata
+//     record, so consumers never touch global memory on the way in.
+//   * each consumer warp owns one head: lanes split a page into
+//     (row group, 16-byte column chunk); partial q.k dots are reduced with a
+//     transpose-reduce (block_size-1 shuffles per page instead of
+//     5 x block_size), then an online softmax in the log2 domain updates the
+//     fp32 accumulator.
+//   * items covering a whole sequence write the output directly; split
+//     sequences leave (m, l, acc) partials in the workspace and a combine
+//     kernel merges them with a log-sum-exp rescale.
+#pragma once
+
+#include <algorithm>
+#include <climits>
+#include <math.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace b2pa {
+
+// Bytes per lane access: the widest of 16/8/4 for which the rows that one
+// warp covers at once (32 / lanes-per-row) fit inside one page.
+constexpr int decode_chunk_bytes(int row_bytes, int bs) {
+  int cands[3] = {16, 8, 4};
+  for (int i = 0; i < 3; ++i) {
+    const int cb = cands[i];
+    if (row_bytes % cb) continue;
+    const int nc = row_bytes / cb;
+    const int lpr = nc < 32 ? nc : 32;
+    if (nc % lpr) continue;
+    if (32 / lpr <= bs) return cb;
+  }
+  return 0;
+}
+
+template <typename T, int D, int BS>
+struct DecodeTile {
+  static constexpr int ES = (int)sizeof(T);
+  static constexpr int ROW_BYTES = D * ES;
+  static constexpr int CB = decode_chunk_bytes(ROW_BYTES, BS);
+  static_assert(CB > 0, "unsupported (head_dim, block_size)");
+  static constexpr int CH = CB / ES;             // elements per lane access
+  static constexpr int NC = D / CH;              // accesses per row
+  static constexpr int LPR = NC < 32 ? NC : 32;  // lanes per row
+  static constexpr int CPL = NC / LPR;           // accesses per lane per row
+  static constexpr int RP = 32 / LPR;            // rows covered at once
+  static constexpr int NR = BS / RP;             // rows per lane per page
+  static_assert(NR >= 1 && NR <= LPR, "row split does not fit the warp");
+  static constexpr int SH = ilog2(LPR) - ilog2(NR);
+  static constexpr int DUP = LPR / NR;           // lanes holding each score
+  static constexpr int HEAD_PAGE_BYTES = BS * ROW_BYTES;
+};
+
+struct DecodeParams {
+  const void* q;
+  int64_t sq_b, sq_h;
+  const void* k_pool;
+  const void* v_pool;
+  int64_t num_blocks;
+  const int32_t* page_table;
+  int64_t pt_stride;
+  int max_pages;
+  const int32_t* seq_lens;
+  const int32_t* cur_lens;
+  void* out;
+  int64_t so_b, so_h;
+  int B, H, G, HG;
+  int pages_per_split;
+  int stages;
+  int stage_bytes;
+  int meta_off;  // offset of StageMeta inside a stage
+  int q_off;     // offset of the fp32 query block inside a stage
+  float qscale;  // scale * log2(e)
+  int32_t* item_off;
+  float* part_ml;
+  float* part_acc;
+  int32_t* status;
+};
+
+struct StageMeta {
+  int b;
+  int h0;
+  int item;
+  int nsplit;
+  int nvalid;  // visible tokens of this page (0 = skip)
+  int flags;
+  int pad[2];
+};
+constexpr int kFirst = 1;
+constexpr int kLast = 2;
+
+// Visible key count of sequence b, clamped to the page table width.
+__device__ __forceinline__ int decode_visible(const DecodeParams& p, int b, int bs) {
+  const int64_t L = p.seq_lens[b];
+  const int64_t c = p.cur_lens[b];
+  int64_t e = L - c + 1;
+  e = e < L ? e : L;
+  if (e < 0) e = 0;
+  const int64_t cap = (int64_t)p.max_pages * bs;
+  if (e > cap) e = cap;
+  return (int)e;
+}
+
+// One CTA: item_off[b] = HG * sum_{b' < b} nsplit(b'), item_off[B] = total.
+template <int BS>
+__global__ void __launch_bounds__(1024) decode_plan_kernel(DecodeParams p) {
+  __shared__ int warp_sums[32];
+  __shared__ int carry;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < p.B; base += 1024) {
+    const int b = base + tid;
+    int n = 0;
+    if (b < p.B) {
+      const int64_t L = p.seq_lens[b];
+      if (L > (int64_t)p.max_pages * BS) set_status(p.status, B2PA_ERR_BAD_BLOCK_ID);
+      const int vis = decode_visible(p, b, BS);
+      const int np = (vis + BS - 1) / BS;
+      int ns = (np + p.pages_per_split - 1) / p.pages_per_split;
+      n = (ns < 1 ? 1 : ns) * p.HG;
+    }
+    int x = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(kFullMask, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[warp] = x;
+    __syncthreads();
+    if (warp == 0) {
+      int w = warp_sums[lane];
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(kFullMask, w, o);
+        if (lane >= o) w += y;
+      }
+      warp_sums[lane] = w;  // inclusive
+    }
+    __syncthreads();
+    const int excl = carry + (warp > 0 ? warp_sums[warp - 1] : 0) + x - n;
+    if (b < p.B) p.item_off[b] = excl;
+    __syncthreads();
+    if (tid == 0) carry += warp_sums[31];
+    __syncthreads();
+  }
+  if (tid == 0) p.item_off[p.B] = carry;
+}
+
+// Reduces v[0..N) over the M lanes (xor masks M/2..1) of a lane group so
+// that lane c ends up with the full sum of element (c >> (log2 M - log2 N)).
+template <int N, int M>
+struct TransposeReduce {
+  __device__ __forceinline__ static float run(float (&v)[N], int c) {
+    if constexpr (M == 1) {
+      return v[0];
+    } else if constexpr (N == 1) {
+      float x = v[0];
+#pragma unroll
+      for (int m = M / 2; m >= 1; m >>= 1) x += __shfl_xor_sync(kFullMask, x, m);
+      return x;
+    } else {
+      constexpr int H = N / 2;
+      constexpr int MASK = M / 2;
+      const bool upper = (c & MASK) != 0;
+      float w[H];
+#pragma unroll
+      for (int k = 0; k < H; ++k) {
+        const float send = upper ? v[k] : v[k + H];
+        const float keep = upper ? v[k + H] : v[k];
+        w[k] = keep + __shfl_xor_sync(kFullMask, send, MASK);
+      }
+      return TransposeReduce<H, M / 2>::run(w, c);
+    }
+  }
+};
+
+template <typename T, int D, int BS>
+__global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
+  using Tile = DecodeTile<T, D, BS>;
+  using V = Vec<T, Tile::CH>;
+  extern __shared__ __align__(128) unsigned char smem[];
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + (size_t)p.stages * p.stage_bytes);
+  uint64_t* empty = full + p.stages;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = p.G;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < p.stages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], G);
+    }
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  const int total = p.item_off[p.B];
+  const int chunk_bytes = G * Tile::HEAD_PAGE_BYTES;
+
+  if (warp == G) {
+    // ------------------------------------------------------------ producer
+    int stage = 0;
+    uint32_t phase = 0;
+    uint32_t issued = 0, issued_par = 0;  // per-stage bookkeeping for drain
+    int cur_b = 0;
+    bool ok = true;
+    for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
+      // Locate the sequence of item w (items are visited in increasing order).
+      while (true) {
+        const int idx = cur_b + 1 + lane;
+        const int v = idx <= p.B ? p.item_off[idx] : INT_MAX;
+        const unsigned m = __ballot_sync(kFullMask, v > w);
+        if (m) {
+          cur_b += __ffs(m) - 1;
+          break;
+        }
+        cur_b += 32;
+      }
+      const int b = cur_b;
+      const int off0 = p.item_off[b];
+      const int nsplit = (p.item_off[b + 1] - off0) / p.HG;
+      const int r = w - off0;
+      const int hg = r / nsplit;
+      const int s = r - hg * nsplit;
+      const int vis = decode_visible(p, b, BS);
+      const int npages = (vis + BS - 1) / BS;
+      const int p0 = s * p.pages_per_split;
+      int p1 = p0 + p.pages_per_split;
+      p1 = p1 < npages ? p1 : npages;
+      const int npg = p1 > p0 ? p1 - p0 : 0;
+      const int count = npg > 0 ? npg : 1;
+      const int h0 = hg * G;
+      const char* kbase = static_cast<const char*>(p.k_pool);
+      const char* vbase = static_cast<const char*>(p.v_pool);
+
+      for (int i0 = 0; i0 < count && ok; i0 += 32) {
+        int blk = -1;
+        if (i0 + lane < npg) {
+          blk = p.page_table[(int64_t)b * p.pt_stride + p0 + i0 + lane];
+          if (blk >= p.num_blocks) {
+            set_status(p.status, B2PA_ERR_BAD_BLOCK_ID);
+            blk = -1;
+          }
+        }
+        const int nj = count - i0 < 32 ? count - i0 : 32;
+        for (int j = 0; j < nj; ++j) {
+          const int bj = __shfl_sync(kFullMask, blk, j);
+          // Every lane waits (and so acquires the consumers' release); the
+          // vote keeps the warp converged if the bounded wait gives up.
+          if (!__all_sync(kFullMask, mbar_wait_bounded(&empty[stage], phase ^ 1, p.status))) {
+            ok = false;
+            break;
+          }
+          unsigned char* st = smem + (size_t)stage * p.stage_bytes;
+          const int pi = i0 + j;
+          if (pi == 0) {
+            // Stage the query of this item, pre-scaled, as fp32.
+            float* qs = reinterpret_cast<float*>(st + p.q_off);
+            const T* qg = static_cast<const T*>(p.q);
+            for (int e = lane; e < G * D; e += 32) {
+              const int hh = e / D;
+              const int d = e - hh * D;
+              qs[e] = to_f32(qg[(int64_t)b * p.sq_b + (int64_t)(h0 + hh) * p.sq_h + d]) * p.qscale;
+            }
+          }
+          if (lane == 0) {
+            StageMeta* meta = reinterpret_cast<StageMeta*>(st + p.meta_off);
+            int nv = 0;
+            if (bj >= 0) {
+              nv = vis - (p0 + pi) * BS;
+              nv = nv < BS ? nv : BS;
+              nv = nv > 0 ? nv : 0;
+            }
+            meta->b = b;
+            meta->h0 = h0;
+            meta->item = w;
+            meta->nsplit = nsplit;
+            meta->nvalid = nv;
+            meta->flags = (pi == 0 ? kFirst : 0) | (pi == count - 1 ? kLast : 0);
+          }
+          __threadfence_block();
+          __syncwarp();
+          if (lane == 0) {
+            if (bj >= 0) {
+              mbar_arrive_expect_tx(&full[stage], 2u * chunk_bytes);
+              const int64_t src = ((int64_t)bj * p.H + h0) * Tile::HEAD_PAGE_BYTES;
+              bulk_g2s(st, kbase + src, chunk_bytes, &full[stage]);
+              bulk_g2s(st + chunk_bytes, vbase + src, chunk_bytes, &full[stage]);
+            } else {
+              mbar_arrive(&full[stage]);
+            }
+          }
+          issued |= 1u << stage;
+          issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
+          if (++stage == p.stages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+    if (!ok && lane == 0) {
+      // Gave up: let every copy this CTA started land before exiting.
+      for (int s2 = 0; s2 < p.stages; ++s2)
+        if (issued & (1u << s2)) mbar_wait_bounded(&full[s2], (issued_par >> s2) & 1u, p.status);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int rg = lane / Tile::LPR;
+  const int c = lane - rg * Tile::LPR;
+  const int r_own = rg + Tile::RP * (c >> Tile::SH);
+  int stage = 0;
+  uint32_t phase = 0;
+  for (int w = blockIdx.x; w < total; w += gridDim.x) {
+    float q[Tile::CPL][Tile::CH];
+    float acc[Tile::CPL][Tile::CH];
+    float m = -INFINITY, l_part = 0.f;
+    while (true) {
+      if (!__all_sync(kFullMask, mbar_wait_bounded(&full[stage], phase, p.status))) return;
+      const unsigned char* st = smem + (size_t)stage * p.stage_bytes;
+      const StageMeta meta = *reinterpret_cast<const StageMeta*>(st + p.meta_off);
+      if (meta.flags & kFirst) {
+        const float* qs = reinterpret_cast<const float*>(st + p.q_off) + warp * D;
+#pragma unroll
+        for (int j = 0; j < Tile::CPL; ++j)
+#pragma unroll
+          for (int e = 0; e < Tile::CH; ++e) {
+            q[j][e] = qs[(c + Tile::LPR * j) * Tile::CH + e];
+            acc[j][e] = 0.f;
+          }
+        m = -INFINITY;
+        l_part = 0.f;
+      }
+      const int nvalid = meta.nvalid;
+      if (nvalid > 0) {
+        const unsigned char* kb = st + warp * Tile::HEAD_PAGE_BYTES;
+        const unsigned char* vb = kb + chunk_bytes;
+        float s[Tile::NR];
+#pragma unroll
+        for (int i = 0; i < Tile::NR; ++i) {
+          const int row = rg + Tile::RP * i;
+          float a = 0.f;
+#pragma unroll
+          for (int j = 0; j < Tile::CPL; ++j) {
+            V kv;
+            kv.w = ld_shared<typename V::Word>(kb + row * Tile::ROW_BYTES + (c + Tile::LPR * j) * Tile::CB);
+            float kf[Tile::CH];
+            kv.to_float(kf);
+#pragma unroll
+            for (int e = 0; e < Tile::CH; ++e) a = fmaf(q[j][e], kf[e], a);
+          }
+          s[i] = a;
+        }
+        float sc = TransposeReduce<Tile::NR, Tile::LPR>::run(s, c);
+        if (r_own >= nvalid) sc = -INFINITY;
+        const float m_new = fmaxf(m, warp_max(sc));
+        const float alpha = exp2f(m - m_new);
+        const float p_own = exp2f(sc - m_new);
+        l_part = l_part * alpha + p_own;
+#pragma unroll
+        for (int j = 0; j < Tile::CPL; ++j)
+#pragma unroll
+          for (int e = 0; e < Tile::CH; ++e) acc[j][e] *= alpha;
+#pragma unroll
+        for (int i = 0; i < Tile::NR; ++i) {
+          const float pi = __shfl_sync(kFullMask, p_own, rg * Tile::LPR + (i << Tile::SH));
+          const int row = rg + Tile::RP * i;
+          if (row < nvalid) {
+#pragma unroll
+            for (int j = 0; j < Tile::CPL; ++j) {
+              V vv;
+              vv.w = ld_shared<typename V::Word>(vb + row * Tile::ROW_BYTES + (c + Tile::LPR * j) * Tile::CB);
+              float vf[Tile::CH];
+              vv.to_float(vf);
+#pragma unroll
+              for (int e = 0; e < Tile::CH; ++e) acc[j][e] = fmaf(pi, vf[e], acc[j][e]);
+            }
+          }
+        }
+        m = m_new;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[stage]);
+      if (++stage == p.stages) {
+        stage = 0;
+        phase ^= 1;
+      }
+      if (meta.flags & kLast) {
+        // Merge the row groups, then the per-lane denominators.
+#pragma unroll
+        for (int mk = Tile::LPR; mk < 32; mk <<= 1)
+#pragma unroll
+          for (int j = 0; j < Tile::CPL; ++j)
+#pragma unroll
+            for (int e = 0; e < Tile::CH; ++e) acc[j][e] += __shfl_xor_sync(kFullMask, acc[j][e], mk);
+        const float l = warp_sum(l_part) * (1.0f / Tile::DUP);
+        const int h = meta.h0 + warp;
+        if (meta.nsplit == 1) {
+          const float den = fmaxf(l, 1e-9f);
+          if (rg == 0) {
+            T* o = static_cast<T*>(p.out) + (int64_t)meta.b * p.so_b + (int64_t)h * p.so_h;
+#pragma unroll
+            for (int j = 0; j < Tile::CPL; ++j) {
+              float f[Tile::CH];
+#pragma unroll
+              for (int e = 0; e < Tile::CH; ++e) f[e] = acc[j][e] / den;
+              V ov;
+              ov.from_float(f);
+              *reinterpret_cast<typename V::Word*>(o + (c + Tile::LPR * j) * Tile::CH) = ov.w;
+            }
+          }
+        } else {
+          const int64_t slot = (int64_t)meta.item * G + warp;
+          if (rg == 0) {
+            float* pa = p.part_acc + slot * D;
+#pragma unroll
+            for (int j = 0; j < Tile::CPL; ++j)
+#pragma unroll
+              for (int e = 0; e < Tile::CH; ++e) pa[(c + Tile::LPR * j) * Tile::CH + e] = acc[j][e];
+          }
+          if (lane == 0) {
+            p.part_ml[2 * slot] = m;
+            p.part_ml[2 * slot + 1] = l;
+          }
+        }
+        break;
+      }
+    }
+  }
+}
+
+// One warp per (sequence, head) whose sequence was split: log-sum-exp merge.
+template <typename T, int D>
+__global__ void __launch_bounds__(256) decode_combine_kernel(DecodeParams p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (gw >= (int64_t)p.B * p.H) return;
+  const int b = (int)(gw / p.H);
+  const int h = (int)(gw - (int64_t)b * p.H);
+  const int off0 = p.item_off[b];
+  const int nsplit = (p.item_off[b + 1] - off0) / p.HG;
+  if (nsplit <= 1) return;
+  const int hg = h / p.G;
+  const int hi = h - hg * p.G;
+  const int64_t base = (int64_t)off0 + (int64_t)hg * nsplit;
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, p.part_ml[2 * ((base + s) * p.G + hi)]);
+  constexpr int PER = D >= 32 ? D / 32 : 1;
+  float o[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) o[i] = 0.f;
+  float L = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const int64_t slot = (base + s) * p.G + hi;
+    const float ms = p.part_ml[2 * slot];
+    const float wgt = (M == -INFINITY) ? 0.f : exp2f(ms - M);
+    L = fmaf(p.part_ml[2 * slot + 1], wgt, L);
+    const float* pa = p.part_acc + slot * D;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int d = lane + 32 * i;
+      if (d < D) o[i] = fmaf(wgt, pa[d], o[i]);
+    }
+  }
+  const float den = fmaxf(L, 1e-9f);
+  T* out = static_cast<T*>(p.out) + (int64_t)b * p.so_b + (int64_t)h * p.so_h;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int d = lane + 32 * i;
+    if (d < D) out[d] = from_f32<T>(o[i] / den);
+  }
+}
+
+int decode_occupancy_cached(const void* func, int threads, size_t smem);
+
+template <typename T, int D, int BS>
+int launch_decode_impl(const AttnArgs& a, const DecodePlan& plan, cudaStream_t stream) {
+  using Tile = DecodeTile<T, D, BS>;
+  DecodeParams p;
+  p.q = a.q;
+  p.sq_b = a.sq[0];
+  p.sq_h = a.sq[1];
+  p.k_pool = a.k_pool;
+  p.v_pool = a.v_pool;
+  p.num_blocks = a.num_blocks;
+  p.page_table = a.page_table;
+  p.pt_stride = a.pt_stride;
+  p.max_pages = a.max_pages;
+  p.seq_lens = a.seq_lens;
+  p.cur_lens = a.cur_lens;
+  p.out = a.out;
+  p.so_b = a.so[0];
+  p.so_h = a.so[1];
+  p.B = a.B;
+  p.H = a.H;
+  p.G = plan.G;
+  p.HG = plan.HG;
+  p.pages_per_split = plan.pages_per_split;
+  p.qscale = a.scale * kLog2e;
+  char* ws = static_cast<char*>(a.workspace);
+  p.item_off = reinterpret_cast<int32_t*>(ws + plan.off_item_off);
+  p.part_ml = reinterpret_cast<float*>(ws + plan.off_part_ml);
+  p.part_acc = reinterpret_cast<float*>(ws + plan.off_part_acc);
+  p.status = a.status;
+
+  const int chunk = plan.G * Tile::HEAD_PAGE_BYTES;
+  p.q_off = 2 * chunk;
+  p.meta_off = p.q_off + plan.G * D * 4;
+  p.stage_bytes = (p.meta_off + (int)sizeof(StageMeta) + 127) / 128 * 128;
+  int stages = (96 * 1024) / p.stage_bytes;
+  stages = std::max(2, std::min(8, stages));
+  const int max_smem = device_max_smem_optin();
+  while (stages > 2 && (size_t)stages * p.stage_bytes + 16 * stages > (size_t)max_smem) --stages;
+  p.stages = stages;
+  const size_t smem = (size_t)stages * p.stage_bytes + 16 * stages;
+  if (smem > (size_t)max_smem)
+    return set_error(B2PA_ERR_UNSUPPORTED, "paged_decode: %zu bytes of shared memory exceed the device limit", smem);
+  const int threads = (plan.G + 1) * 32;
+
+  auto kern = paged_decode_kernel<T, D, BS>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_decode smem attribute: %s", cudaGetErrorString(e));
+  const int per_sm = decode_occupancy_cached(reinterpret_cast<const void*>(kern), threads, smem);
+  if (per_sm <= 0) return set_error(B2PA_ERR_UNSUPPORTED, "paged_decode: kernel does not fit on an SM");
+  int64_t grid = (int64_t)device_sm_count() * per_sm;
+  if (grid > plan.max_items) grid = plan.max_items;
+  if (grid < 1) grid = 1;
+
+  decode_plan_kernel<BS><<<1, 1024, 0, stream>>>(p);
+  kern<<<(unsigned)grid, threads, smem, stream>>>(p);
+  const int64_t warps = (int64_t)a.B * a.H;
+  const unsigned cgrid = (unsigned)((warps + 7) / 8);
+  decode_combine_kernel<T, D><<<cgrid, 256, 0, stream>>>(p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_decode launch: %s", cudaGetErrorString(e));
+  return B2PA_OK;
+}
+
+template <typename T>
+int dispatch_decode(const AttnArgs& a, const DecodePlan& plan, cudaStream_t s) {
+#define B2PA_DEC_CASE(DD, BB) \
+  if (a.D == DD && a.block_size == BB) return launch_decode_impl<T, DD, BB>(a, plan, s);
+#define B2PA_DEC_D(DD) B2PA_DEC_CASE(DD, 8) B2PA_DEC_CASE(DD, 16) B2PA_DEC_CASE(DD, 32)
+  B2PA_DEC_D(16)
+  B2PA_DEC_D(32)
+  B2PA_DEC_D(64)
+  B2PA_DEC_D(128)
+  B2PA_DEC_D(256)
+#undef B2PA_DEC_D
+#undef B2PA_DEC_CASE
+  return set_error(B2PA_ERR_UNSUPPORTED, "paged_decode: head_dim %d / block_size %d not built", a.D, a.block_size);
+}
+
+}  // namespace b2pa

@@ -1,0 +1,171 @@
+/*
+ * b2pa.h -- C ABI of the B200 paged-attention backend (libb2pa.so).
+ *
+ * The library replaces three pieces of the reference serving stack
+ * (jacobzhang22/efficient-inference-system):
+ *
+ *   - the per-token KV append/scatter into a layer's block pool
+ *       src/cache/paged_kv.py:102-120 (PagedKVCacheState.append)
+ *       src/cache/paged_kv.py:151-172 (BatchedPagedKVCache.append_batch)
+ *   - the single-query paged decode attention launcher + kernel
+ *       src/kernels/triton_paged_attention.py:10-85, 179-217
+ *   - the chunked-prefill paged attention launcher + kernel
+ *       src/kernels/triton_paged_attention.py:88-176, 220-258
+ *
+ * Data layout (unchanged from the reference, src/cache/paged_kv.py:54-62):
+ *   k_pool, v_pool : [num_blocks, H, block_size, D], contiguous, dtype of q
+ *   page_table     : int32 [B, max_pages], -1 padded (paged_kv.py:174-193)
+ *   seq_lens       : int32 [B], length of each sequence AFTER the append
+ *   cur_lens       : int32 [B], tokens added by this forward (attention.py:56-62)
+ *   q, out         : [B, H, T, D] with arbitrary B/H/T strides, unit D stride
+ *
+ * Attention semantics (src/kernels/reference_paged_attention.py:31-57):
+ *   query row t of sequence b sits at absolute position
+ *       pos = seq_lens[b] - cur_lens[b] + t
+ *   and sees keys 0 .. min(seq_lens[b], pos + 1) - 1.  Rows that see no key
+ *   produce zeros.  out = softmax(q.K^T * scale) . V, accumulated in fp32,
+ *   stored in the dtype of q.
+ *
+ * Conventions:
+ *   - every entry point returns 0 (B2PA_OK) or a negative b2pa_status; no C++
+ *     exception crosses the ABI.  b2pa_last_error_string() describes the most
+ *     recent failure of the calling thread.
+ *   - all pointers except `strides` arrays are DEVICE pointers owned by the
+ *     caller; the library borrows them for the duration of the (asynchronous)
+ *     call on `stream` (a cudaStream_t, NULL = legacy default stream).
+ *   - the library never allocates device memory.  Scratch space is passed in
+ *     as `workspace` (size from the matching *_workspace_size function).
+ *   - `status` (nullable) is a device int32 that kernels set (first error
+ *     wins) when they detect a fault they survived: an out-of-range block id
+ *     or a bounded wait that gave up.  Read it with b2pa_status_read().
+ *   - pool pointers are re-read on every call: the reference pool grows with
+ *     torch.cat (paged_kv.py:64-69), which moves the tensors.
+ */
+#ifndef B2PA_H_
+#define B2PA_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2PA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define B2PA_API __attribute__((visibility("default")))
+#else
+#define B2PA_API
+#endif
+
+typedef enum b2pa_dtype {
+  B2PA_DTYPE_F32 = 0,
+  B2PA_DTYPE_BF16 = 1,
+  B2PA_DTYPE_F16 = 2
+} b2pa_dtype;
+
+typedef enum b2pa_status {
+  B2PA_OK = 0,
+  B2PA_ERR_INVALID_ARGUMENT = -1,  /* null pointer, negative size, bad stride */
+  B2PA_ERR_UNSUPPORTED = -2,       /* dtype / head_dim / block_size not built */
+  B2PA_ERR_BAD_BLOCK_ID = -3,      /* (device) page-table entry >= num_blocks */
+  B2PA_ERR_WORKSPACE = -4,         /* workspace missing or too small */
+  B2PA_ERR_CUDA = -5,              /* a CUDA runtime call failed */
+  B2PA_ERR_DEVICE_TIMEOUT = -6     /* (device) a bounded wait gave up */
+} b2pa_status;
+
+/* ABI version of the loaded library (B2PA_ABI_VERSION at build time). */
+B2PA_API int b2pa_abi_version(void);
+
+/* Description of the calling thread's most recent error ("" if none). */
+B2PA_API const char* b2pa_last_error_string(void);
+
+/* Copies the device status word to *host_status (synchronises `stream`). */
+B2PA_API int b2pa_status_read(const int32_t* status, int32_t* host_status, void* stream);
+
+/* Clears the device status word (asynchronous on `stream`). */
+B2PA_API int b2pa_status_clear(int32_t* status, void* stream);
+
+/*
+ * KV append / scatter.  Replaces the slice copies of
+ * PagedKVCacheState.append (src/cache/paged_kv.py:109-120) for a whole batch
+ * (BatchedPagedKVCache.append_batch, paged_kv.py:151-172) in one launch.
+ *
+ * For each sequence b and t < min(lengths[b], T):
+ *   pos = start_pos[b] + t
+ *   blk = page_table[b * pt_stride + pos / block_size]
+ *   k_pool[blk, h, pos % block_size, :] = k_new[b, h, t, :]   (all h)
+ *   v_pool[...]                          = v_new[b, h, t, :]
+ * Block ids must already be allocated by the caller's host allocator in the
+ * reference order (paged_kv.py:110-113); this kernel only copies, bit-exact.
+ * new_k_strides / new_v_strides / pool_strides are element strides of the
+ * [B,H,T,D] and [num_blocks,H,block_size,D] tensors.
+ */
+B2PA_API int b2pa_kv_append(const void* k_new, const int64_t new_k_strides[4],
+                   const void* v_new, const int64_t new_v_strides[4],
+                   void* k_pool, void* v_pool, const int64_t pool_strides[4],
+                   int64_t num_blocks,
+                   const int32_t* page_table, int64_t pt_stride, int max_pages,
+                   const int32_t* start_pos, const int32_t* lengths,
+                   int B, int H, int T, int D, int block_size, int dtype,
+                   int32_t* status, void* stream);
+
+/*
+ * Workspace bytes b2pa_paged_decode needs for this problem size.  Replaces
+ * nothing in the reference (the Triton decode kernel runs one program per
+ * (seq, head) with no split, triton_paged_attention.py:189); the split-K
+ * partials of this backend live here.
+ */
+B2PA_API size_t b2pa_paged_decode_workspace_size(int B, int H, int D, int max_pages,
+                                        int block_size, int dtype);
+
+/*
+ * Single-query paged decode attention (T == 1).  Replaces
+ * paged_attention_decode_triton, src/kernels/triton_paged_attention.py:179-217.
+ * q_strides / out_strides: element strides of [B,H,1,D] (D stride must be 1).
+ */
+B2PA_API int b2pa_paged_decode(const void* q, const int64_t q_strides[4],
+                      const void* k_pool, const void* v_pool,
+                      const int64_t pool_strides[4], int64_t num_blocks,
+                      const int32_t* page_table, int64_t pt_stride, int max_pages,
+                      const int32_t* seq_lens, const int32_t* cur_lens,
+                      void* out, const int64_t out_strides[4],
+                      int B, int H, int D, int block_size, float scale, int dtype,
+                      void* workspace, size_t workspace_bytes,
+                      int32_t* status, void* stream);
+
+/* Workspace bytes b2pa_paged_prefill needs (0 for the paths that need none). */
+B2PA_API size_t b2pa_paged_prefill_workspace_size(int B, int H, int T, int D, int max_pages,
+                                         int block_size, int dtype);
+
+/*
+ * Chunked-prefill paged attention (any T >= 1, padded rows included).
+ * Replaces paged_attention_prefill_triton,
+ * src/kernels/triton_paged_attention.py:220-258.
+ */
+B2PA_API int b2pa_paged_prefill(const void* q, const int64_t q_strides[4],
+                       const void* k_pool, const void* v_pool,
+                       const int64_t pool_strides[4], int64_t num_blocks,
+                       const int32_t* page_table, int64_t pt_stride, int max_pages,
+                       const int32_t* seq_lens, const int32_t* cur_lens,
+                       void* out, const int64_t out_strides[4],
+                       int B, int H, int T, int D, int block_size, float scale,
+                       int dtype, void* workspace, size_t workspace_bytes,
+                       int32_t* status, void* stream);
+
+/*
+ * Zeroes whole blocks of both pools in one launch.  Replaces the per-block
+ * k_blocks[id].zero_() / v_blocks[id].zero_() pair of
+ * LayerBlockPool.release_block, src/cache/paged_kv.py:80-85.
+ */
+B2PA_API int b2pa_zero_blocks(void* k_pool, void* v_pool, const int64_t pool_strides[4],
+                     int64_t num_blocks, const int32_t* block_ids, int n_ids,
+                     int H, int D, int block_size, int dtype,
+                     int32_t* status, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* B2PA_H_ */

@@ -1,0 +1,165 @@
+"""Generates the golden vectors in tests/golden/*.npz by running the
+reference implementation itself (jacobzhang22/efficient-inference-system).
+
+Run here, where the reference checkout is available (read-only):
+
+    python tests/golden/make_golden.py --reference /path/to/reference
+
+Every case drives the reference's own public API on CPU:
+``LayerBlockPool`` / ``PagedKVCacheState`` / ``BatchedPagedKVCache.append_batch``
+(src/cache/paged_kv.py) for pools and block tables, and
+``paged_attention_reference`` (src/kernels/reference_paged_attention.py) for
+attention outputs.  The fixtures are small and committed; the GPU box never
+needs the reference.
+"""
+from __future__ import annotations
+
+import argparse
+import sys
+from pathlib import Path
+
+import numpy as np
+import torch
+
+OUT_DIR = Path(__file__).resolve().parent
+
+
+def _import_reference(path: str):
+    sys.path.insert(0, path)
+    from src.cache.paged_kv import BatchedPagedKVCache, LayerBlockPool, PagedKVCacheState
+    from src.kernels.reference_paged_attention import paged_attention_reference
+    return BatchedPagedKVCache, LayerBlockPool, PagedKVCacheState, paged_attention_reference
+
+
+def _tables(states) -> tuple[np.ndarray, np.ndarray]:
+    flat = np.array([b for s in states for b in s.block_ids], dtype=np.int32)
+    counts = np.array([len(s.block_ids) for s in states], dtype=np.int32)
+    return flat, counts
+
+
+def case_alloc_sequence(ref) -> dict:
+    """Allocator growth, block-boundary appends, clamping, release + LIFO reuse."""
+    Batched, Pool, State, _ = ref
+    torch.manual_seed(1)
+    pool = Pool(block_size=4, initial_blocks=2, growth_factor=2.0)
+    states = [State(pool=pool) for _ in range(3)]
+    cache = Batched(states=states, pool=pool)
+    H, D = 2, 8
+    steps = [
+        (6, torch.tensor([6, 1, 0]), None),
+        (1, None, None),
+        (5, [5, 4, 3], 1),          # release state 1 before this append
+        (3, 7, None),               # int length larger than T: clamped to T
+        (4, torch.tensor([0, 4, 2]), None),
+    ]
+    rec: dict = {"H": H, "D": D, "block_size": 4, "initial_blocks": 2, "growth_factor": 2.0,
+                 "n_steps": len(steps)}
+    for i, (T, lens, release_idx) in enumerate(steps):
+        if release_idx is not None:
+            states[release_idx].release()
+        k = torch.randn(3, H, T, D)
+        v = torch.randn(3, H, T, D)
+        if isinstance(lens, list):
+            lens_arg = torch.tensor(lens)
+        else:
+            lens_arg = lens
+        ret = cache.append_batch(k, v, current_lengths=lens_arg)
+        flat, counts = _tables(states)
+        rec[f"step{i}_T"] = T
+        rec[f"step{i}_lens_kind"] = "none" if lens is None else ("int" if isinstance(lens, int) else "list")
+        rec[f"step{i}_lens"] = np.array([0, 0, 0] if lens is None else ([lens] * 3 if isinstance(lens, int) else
+                                        [int(x) for x in (lens.tolist() if torch.is_tensor(lens) else lens)]),
+                                        dtype=np.int64)
+        rec[f"step{i}_release"] = -1 if release_idx is None else release_idx
+        rec[f"step{i}_k"] = k.numpy()
+        rec[f"step{i}_v"] = v.numpy()
+        rec[f"step{i}_ret"] = ret.numpy()
+        rec[f"step{i}_block_ids"] = flat
+        rec[f"step{i}_block_counts"] = counts
+        rec[f"step{i}_free"] = np.array(pool.free_block_ids, dtype=np.int32)
+        rec[f"step{i}_capacity"] = pool.capacity_blocks
+    rec["k_pool"] = pool.k_blocks.numpy()
+    rec["v_pool"] = pool.v_blocks.numpy()
+    return rec
+
+
+def _attention_case(ref, *, seed, B, H, D, bs, initial_blocks, prefix, T, cur, dtype=torch.float32) -> dict:
+    """Prefix append, chunk append, then paged_attention_reference."""
+    Batched, Pool, State, attn = ref
+    torch.manual_seed(seed)
+    pool = Pool(block_size=bs, initial_blocks=initial_blocks, growth_factor=2.0)
+    states = [State(pool=pool) for _ in range(B)]
+    cache = Batched(states=states, pool=pool)
+    Tp = max(max(prefix), 1)
+    kp = torch.randn(B, H, Tp, D).to(dtype)
+    vp = torch.randn(B, H, Tp, D).to(dtype)
+    cache.append_batch(kp, vp, current_lengths=torch.tensor(prefix))
+    kc = torch.randn(B, H, T, D).to(dtype)
+    vc = torch.randn(B, H, T, D).to(dtype)
+    q = torch.randn(B, H, T, D).to(dtype)
+    cur_t = torch.tensor(cur)
+    cache.append_batch(kc, vc, current_lengths=cur_t)
+    flat, counts = _tables(states)
+    seq_lens = np.array([s.seq_len for s in states], dtype=np.int32)
+    if dtype == torch.float32:
+        out = attn(q=q, kv_cache=cache, current_lengths=cur_t)
+        pool_k, pool_v, q_np = pool.k_blocks.numpy(), pool.v_blocks.numpy(), q.numpy()
+    else:
+        # bf16: the reference computes on the same bf16 values upcast to fp32.
+        kb, vb = pool.k_blocks, pool.v_blocks
+        pool.k_blocks, pool.v_blocks = kb.float(), vb.float()
+        out = attn(q=q.float(), kv_cache=cache, current_lengths=cur_t)
+        pool.k_blocks, pool.v_blocks = kb, vb
+        pool_k = kb.view(torch.int16).numpy().view(np.uint16)
+        pool_v = vb.view(torch.int16).numpy().view(np.uint16)
+        q_np = q.view(torch.int16).numpy().view(np.uint16)
+        kc = kc.float()
+    return {
+        "B": B, "H": H, "D": D, "block_size": bs, "T": T, "dtype": str(dtype).replace("torch.", ""),
+        "prefix": np.array(prefix, dtype=np.int32), "cur_lens": np.array(cur, dtype=np.int32),
+        "seq_lens": seq_lens, "block_ids": flat, "block_counts": counts,
+        "k_pool": pool_k, "v_pool": pool_v, "q": q_np, "out": out.float().numpy(),
+        "k_chunk": kc.numpy() if dtype == torch.float32 else kc.numpy(),
+    }
+
+
+CASES = {
+    "alloc_sequence": case_alloc_sequence,
+    "decode_f32_bs8_d16": lambda ref: _attention_case(ref, seed=2, B=4, H=2, D=16, bs=8, initial_blocks=4,
+                                                      prefix=[0, 7, 8, 23], T=1, cur=[1, 1, 1, 1]),
+    "decode_f32_curvar": lambda ref: _attention_case(ref, seed=3, B=4, H=2, D=32, bs=16, initial_blocks=4,
+                                                     prefix=[0, 15, 16, 40], T=1, cur=[1, 0, 2, 1]),
+    "decode_f32_bs16_d64": lambda ref: _attention_case(ref, seed=4, B=2, H=4, D=64, bs=16, initial_blocks=8,
+                                                       prefix=[128, 199], T=1, cur=[1, 1]),
+    "prefill_f32_bs16_d32": lambda ref: _attention_case(ref, seed=5, B=3, H=2, D=32, bs=16, initial_blocks=4,
+                                                        prefix=[0, 5, 20], T=12, cur=[12, 7, 0]),
+    "prefill_f32_bs8_d16": lambda ref: _attention_case(ref, seed=6, B=2, H=4, D=16, bs=8, initial_blocks=8,
+                                                       prefix=[3, 17], T=24, cur=[24, 9]),
+    "prefill_bf16_bs16_d64": lambda ref: _attention_case(ref, seed=7, B=2, H=2, D=64, bs=16, initial_blocks=8,
+                                                         prefix=[10, 40], T=20, cur=[20, 13],
+                                                         dtype=torch.bfloat16),
+    "decode_bf16_bs16_d128": lambda ref: _attention_case(ref, seed=8, B=3, H=2, D=128, bs=16, initial_blocks=8,
+                                                         prefix=[1, 31, 64], T=1, cur=[1, 1, 1],
+                                                         dtype=torch.bfloat16),
+}
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--only", default=None)
+    args = ap.parse_args()
+    torch.set_num_threads(1)
+    ref = _import_reference(args.reference)
+    for name, fn in CASES.items():
+        if args.only and name != args.only:
+            continue
+        rec = fn(ref)
+        path = OUT_DIR / f"{name}.npz"
+        np.savez_compressed(path, **{k: np.asarray(v) for k, v in rec.items()})
+        print(f"wrote {path} ({path.stat().st_size} bytes)")
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,116 @@
+"""The C ABI library on CPU: it loads, exports every symbol include/b2pa.h
+declares, and rejects bad arguments with status codes before touching the
+GPU.  No kernel runs here."""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+from pathlib import Path
+
+import pytest
+
+from b2pa import _lib
+
+REPO = Path(__file__).resolve().parent.parent
+HEADER = REPO / "include" / "b2pa.h"
+
+
+def _declared() -> list[str]:
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"B2PA_API\s+[\w\s\*]+?\b(b2pa_\w+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not _lib.LIB_PATH.exists():
+        import __graft_entry__  # noqa: F401  (repo root on sys.path)
+
+        __graft_entry__.build()
+    return _lib.load()
+
+
+def test_header_declares_the_abi():
+    names = _declared()
+    assert "b2pa_paged_decode" in names and "b2pa_kv_append" in names and "b2pa_paged_prefill" in names
+    assert len(names) >= 10
+
+
+def test_every_declared_symbol_is_exported_and_bound(lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIB_PATH)], capture_output=True, text=True,
+                         check=True).stdout
+    exported = set(re.findall(r"\bT (b2pa_\w+)", out))
+    for name in _declared():
+        assert name in exported, f"{name} declared in b2pa.h but not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes binding"
+        assert getattr(lib, name) is not None
+
+
+def test_abi_version(lib):
+    m = re.search(r"#define B2PA_ABI_VERSION (\d+)", HEADER.read_text())
+    assert lib.b2pa_abi_version() == int(m.group(1))
+
+
+def test_status_codes_match_header():
+    text = HEADER.read_text()
+    for code, name in _lib.STATUS_NAMES.items():
+        assert re.search(rf"{name}\s*=\s*{code}\b", text), name
+
+
+def _decode(lib, **kw):
+    args = dict(q=4096, qs=(64, 64, 64, 1), kp=16, vp=16, ps=(16 * 64, 16 * 64, 64, 1), nb=10, pt=8, pts=4,
+                mp=4, sl=8, cl=8, out=8192, os=(64, 64, 64, 1), B=1, H=1, D=64, bs=16, dt=0, ws=256, wsb=1 << 30)
+    args.update(kw)
+    i64 = lambda t: (ctypes.c_int64 * 4)(*t)
+    return lib.b2pa_paged_decode(args["q"], i64(args["qs"]), args["kp"], args["vp"], i64(args["ps"]), args["nb"],
+                                 args["pt"], args["pts"], args["mp"], args["sl"], args["cl"], args["out"],
+                                 i64(args["os"]), args["B"], args["H"], args["D"], args["bs"], 0.125, args["dt"],
+                                 args["ws"], args["wsb"], None, None)
+
+
+def test_decode_argument_validation(lib):
+    assert _decode(lib, H=0) == -1
+    assert _decode(lib, dt=7) == -2
+    assert _decode(lib, D=48, ps=(16 * 48, 16 * 48, 48, 1)) == -2
+    assert _decode(lib, bs=12) == -2
+    assert _decode(lib, ps=(1, 16 * 64, 64, 1)) == -2            # pools not contiguous
+    assert _decode(lib, qs=(64, 64, 64, 2)) == -2                # non-unit D stride
+    assert _decode(lib, q=0) == -1                               # null q
+    assert _decode(lib, pts=2) == -1                             # row stride < max_pages
+    assert _decode(lib, wsb=16) == -4                            # workspace too small
+    assert _decode(lib, ws=0) == -4                              # missing workspace
+    assert _decode(lib, B=0) == 0                                # empty batch: nothing to do
+    assert "workspace" in _lib.last_error() or _lib.last_error() == ""
+
+
+def test_workspace_size_is_monotone(lib):
+    f = lib.b2pa_paged_decode_workspace_size
+    a = f(64, 8, 64, 65, 16, 0)
+    b = f(64, 8, 64, 130, 16, 0)
+    c = f(512, 32, 128, 513, 16, 1)
+    assert 0 < a <= b
+    assert c > 0 and c % 256 == 0
+    assert f(0, 8, 64, 65, 16, 0) == 0
+    assert lib.b2pa_paged_prefill_workspace_size(8, 8, 256, 64, 64, 16, 0) == 0
+
+
+def test_append_and_zero_argument_validation(lib):
+    i64 = lambda t: (ctypes.c_int64 * 4)(*t)
+    ok = (256, 64, 64, 1)
+    pool = (8 * 16 * 64, 16 * 64, 64, 1)
+    rc = lib.b2pa_kv_append(8, i64(ok), 8, i64(ok), 16, 16, i64((1, 1, 1, 1)), 10, 8, 4, 4, 8, 8, 1, 8, 1, 64, 16, 0,
+                            None, None)
+    assert rc == -2
+    rc = lib.b2pa_kv_append(8, i64(ok), 8, i64(ok), 16, 16, i64(pool), 10, 8, 4, 4, 8, 8, 1, 8, 1, 64, 16, 9, None, None)
+    assert rc == -2
+    rc = lib.b2pa_kv_append(8, i64(ok), 8, i64(ok), 16, 16, i64(pool), 10, 8, 4, 4, 8, 8, 0, 8, 1, 64, 16, 0, None, None)
+    assert rc == 0
+    assert lib.b2pa_zero_blocks(16, 16, i64(pool), 10, 8, -1, 8, 64, 16, 0, None, None) == -1
+    assert lib.b2pa_zero_blocks(16, 16, i64(pool), 10, 8, 0, 8, 64, 16, 0, None, None) == 0
+
+
+def test_missing_library_raises(monkeypatch, tmp_path):
+    monkeypatch.setattr(_lib, "_lib", None)
+    monkeypatch.setenv("B2PA_LIB", str(tmp_path / "nope.so"))
+    with pytest.raises(RuntimeError, match="not found"):
+        _lib.load()

@@ -1,0 +1,136 @@
+"""Host-side logic of the b2pa package, on CPU: block allocation order,
+growth, release/reuse, page tables and error behaviour.  Pools live on the
+``meta`` device, so no data moves and no kernel is needed.  The allocation
+results are pinned against the reference's own (tests/golden/alloc_sequence)."""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import b2pa
+from b2pa.paged_kv import plan_append
+from tests._helpers import load_golden
+
+META = torch.device("meta")
+
+
+def _meta(*shape):
+    return torch.empty(*shape, device=META)
+
+
+def test_allocation_sequence_matches_reference():
+    g = load_golden("alloc_sequence")
+    pool = b2pa.LayerBlockPool(int(g["block_size"]), int(g["initial_blocks"]), float(g["growth_factor"]))
+    states = [b2pa.PagedKVCacheState(pool=pool) for _ in range(3)]
+    cache = b2pa.BatchedPagedKVCache(states=states, pool=pool)
+    H, D = int(g["H"]), int(g["D"])
+    for i in range(int(g["n_steps"])):
+        rel = int(g[f"step{i}_release"])
+        if rel >= 0:
+            states[rel].release()
+        T = int(g[f"step{i}_T"])
+        kind = str(g[f"step{i}_lens_kind"])
+        lens = None if kind == "none" else (int(g[f"step{i}_lens"][0]) if kind == "int" else
+                                            torch.tensor(g[f"step{i}_lens"]))
+        ret = cache.append_batch(_meta(3, H, T, D), _meta(3, H, T, D), lens)
+        assert ret.dtype == torch.long
+        assert [s.seq_len for s in states] == g[f"step{i}_ret"].tolist()
+        assert [b for s in states for b in s.block_ids] == g[f"step{i}_block_ids"].tolist()
+        assert [len(s.block_ids) for s in states] == g[f"step{i}_block_counts"].tolist()
+        assert pool.free_block_ids == g[f"step{i}_free"].tolist()
+        assert pool.capacity_blocks == int(g[f"step{i}_capacity"])
+        assert tuple(pool.k_blocks.shape) == (pool.capacity_blocks, H, int(g["block_size"]), D)
+
+
+# The reference's own unit tests (tests/test_paged_kv.py:9-40), on meta pools.
+def test_allocator_growth_and_reuse():
+    pool = b2pa.LayerBlockPool(block_size=4, initial_blocks=1, growth_factor=2.0)
+    state = b2pa.PagedKVCacheState(pool=pool)
+    b2pa.BatchedPagedKVCache([state], pool=pool).append_batch(_meta(1, 2, 6, 8), _meta(1, 2, 6, 8), [6])
+    assert pool.capacity_blocks >= 2
+    allocated = list(state.block_ids)
+    state.release()
+    assert pool.allocate_block() in allocated
+
+
+def test_block_boundary_append():
+    pool = b2pa.LayerBlockPool(block_size=4, initial_blocks=2, growth_factor=2.0)
+    state = b2pa.PagedKVCacheState(pool=pool)
+    b2pa.BatchedPagedKVCache([state], pool=pool).append_batch(_meta(1, 2, 5, 8), _meta(1, 2, 5, 8), [5])
+    assert state.seq_len == 5
+    assert len(state.block_ids) == 2
+
+
+def test_batched_page_table_handles_heterogeneous_lengths():
+    pool = b2pa.LayerBlockPool(block_size=4, initial_blocks=4, growth_factor=2.0)
+    states = [b2pa.PagedKVCacheState(pool=pool) for _ in range(2)]
+    batch = b2pa.BatchedPagedKVCache(states=states, pool=pool)
+    batch.append_batch(_meta(2, 2, 4, 8), _meta(2, 2, 4, 8), current_lengths=torch.tensor([4, 2]))
+    table = batch.page_table_array()
+    assert table.shape == (2, 1)
+    assert [s.seq_len for s in states] == [4, 2]
+
+
+@pytest.mark.parametrize("bs", [8, 16, 32])
+def test_block_boundaries_allocate_exactly(bs):
+    pool = b2pa.LayerBlockPool(block_size=bs, initial_blocks=1, growth_factor=2.0)
+    st = b2pa.PagedKVCacheState(pool=pool)
+    cache = b2pa.BatchedPagedKVCache([st], pool=pool)
+    total = 0
+    for n in [1, bs - 1, 1, bs, bs + 1, 0, 3 * bs - 2]:
+        cache.append_batch(_meta(1, 1, max(n, 1), 16), _meta(1, 1, max(n, 1), 16), [n])
+        total += n
+        assert st.seq_len == total
+        assert len(st.block_ids) == -(-total // bs)
+    assert len(set(st.block_ids)) == len(st.block_ids)
+
+
+def test_page_table_padding_and_empty():
+    pool = b2pa.LayerBlockPool(block_size=16, initial_blocks=4, growth_factor=2.0)
+    states = [b2pa.PagedKVCacheState(pool=pool) for _ in range(3)]
+    cache = b2pa.BatchedPagedKVCache(states, pool=pool)
+    assert cache.page_table_array().shape == (3, 0)
+    cache.append_batch(_meta(3, 2, 40, 16), _meta(3, 2, 40, 16), [40, 0, 17])
+    t = cache.page_table_array()
+    assert t.dtype == np.int32 and t.shape == (3, 3)
+    assert (t[1] == -1).all() and t[2, 2] == -1 and (t[0] >= 0).all()
+    start = plan_append(cache, _meta(3, 2, 1, 16), [1, 1, 1])
+    assert start == [40, 0, 17]
+
+
+def test_states_must_share_the_pool():
+    p1 = b2pa.LayerBlockPool(16, 4, 2.0)
+    p2 = b2pa.LayerBlockPool(16, 4, 2.0)
+    cache = b2pa.BatchedPagedKVCache([b2pa.PagedKVCacheState(pool=p1), b2pa.PagedKVCacheState(pool=p2)], pool=p1)
+    with pytest.raises(ValueError):
+        cache.append_batch(_meta(2, 1, 1, 16), _meta(2, 1, 1, 16), 1)
+
+
+def test_no_cpu_path():
+    pool = b2pa.LayerBlockPool(16, 4, 2.0)
+    cache = b2pa.BatchedPagedKVCache([b2pa.PagedKVCacheState(pool=pool)], pool=pool)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        cache.append_batch(torch.zeros(1, 2, 1, 16), torch.zeros(1, 2, 1, 16), 1)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        b2pa.paged_attention("b200_paged", torch.zeros(1, 2, 1, 16), cache, 1)
+
+
+def test_backend_name_is_validated_like_the_reference():
+    pool = b2pa.LayerBlockPool(16, 4, 2.0)
+    cache = b2pa.BatchedPagedKVCache([b2pa.PagedKVCacheState(pool=pool)], pool=pool)
+    with pytest.raises(ValueError, match="Unsupported paged attention backend"):
+        b2pa.paged_attention("flash", torch.zeros(1, 2, 1, 16), cache, 1)
+    assert "triton_paged" in b2pa.SUPPORTED_BACKENDS and "b200_paged" in b2pa.SUPPORTED_BACKENDS
+
+
+def test_memory_accounting_matches_reference_formulas():
+    pool = b2pa.LayerBlockPool(block_size=16, initial_blocks=4, growth_factor=2.0)
+    st = b2pa.PagedKVCacheState(pool=pool)
+    b2pa.BatchedPagedKVCache([st], pool=pool).append_batch(_meta(1, 8, 20, 64), _meta(1, 8, 20, 64), [20])
+    es = 4
+    assert pool.bytes_per_block() == 2 * 8 * 16 * 64 * es
+    assert pool.reserved_bytes() == 4 * pool.bytes_per_block()
+    assert st.live_bytes() == 20 * 8 * 64 * 2 * es
+    assert st.reserved_bytes() == 2 * pool.bytes_per_block()
+    assert st.fragmentation_bytes() == st.reserved_bytes() - st.live_bytes()
