@@ -135,6 +135,30 @@ B2PA_API int b2pa_paged_decode(const void* q, const int64_t q_strides[4],
                       void* workspace, size_t workspace_bytes,
                       int32_t* status, void* stream);
 
+/*
+ * Decode without a caller workspace.  No counterpart in the reference: this
+ * entry point exists for callers that cannot allocate device memory (a host
+ * callback or real-time thread that must not block on the allocator, a
+ * plugin whose host framework owns all device memory, a process whose
+ * footprint is fixed at start-up).  Same arguments and results as
+ * b2pa_paged_decode without `workspace`; the scratch lives in a fixed array
+ * of B2PA_NOALLOC_SCRATCH_BYTES inside the library, held on every GPU that
+ * loads it until exit.  Problems whose b2pa_paged_decode_workspace_size()
+ * exceeds that return B2PA_ERR_WORKSPACE.  All calls on a device share the
+ * array: calls that may overlap on the GPU (unordered streams) race.  The
+ * first call on each device looks the array up (cudaGetSymbolAddress), so
+ * make it before any stream capture.  Allocates nothing.
+ */
+#define B2PA_NOALLOC_SCRATCH_BYTES (32u << 20)
+B2PA_API int b2pa_paged_decode_noalloc(const void* q, const int64_t q_strides[4],
+                      const void* k_pool, const void* v_pool,
+                      const int64_t pool_strides[4], int64_t num_blocks,
+                      const int32_t* page_table, int64_t pt_stride, int max_pages,
+                      const int32_t* seq_lens, const int32_t* cur_lens,
+                      void* out, const int64_t out_strides[4],
+                      int B, int H, int D, int block_size, float scale, int dtype,
+                      int32_t* status, void* stream);
+
 /* Workspace bytes b2pa_paged_prefill needs (0 for the paths that need none). */
 B2PA_API size_t b2pa_paged_prefill_workspace_size(int B, int H, int T, int D, int max_pages,
                                          int block_size, int dtype);
