@@ -39,10 +39,9 @@ def _attn_call(fn_name: str, q, k_pool, v_pool, page_table, seq_lens, current_le
     out = torch.empty_like(q)
     if max_pages is None:
         max_pages = page_table.shape[1]
-    pt_stride = page_table.stride(0) if page_table.dim() == 2 and page_table.numel() else max(max_pages, 1)
     if page_table.numel() and page_table.stride(1) != 1:
         page_table = page_table.contiguous()
-        pt_stride = page_table.stride(0)
+    pt_stride = page_table.stride(0) if page_table.dim() == 2 and page_table.numel() else max(max_pages, 1)
     seq_lens = seq_lens.to(dtype=torch.int32)
     cur = current_lengths.to(dtype=torch.int32)
     dev = q.device

@@ -28,6 +28,7 @@ import numpy as np
 import torch
 
 from . import _lib
+from ._metadata import block_table_and_lengths
 from ._staging import stage_int32
 
 
@@ -263,7 +264,8 @@ def append_batch_into(cache, k_new: torch.Tensor, v_new: torch.Tensor, current_l
         raise RuntimeError("b2pa: k_new must be a CUDA tensor (this package has no CPU path)")
     starts = plan_append(cache, k_new, clamped)
     if any(clamped) and k_new.device.type == "cuda":
-        _kv_append(cache, k_new, v_new, starts, clamped)
+        seq_lens = _kv_append(cache, k_new, v_new, starts, clamped)
+        return seq_lens.to(torch.long)
     return torch.tensor([s.seq_len for s in cache.states], dtype=torch.long, device=k_new.device)
 
 
@@ -274,39 +276,12 @@ def _require_cuda(t: torch.Tensor, what: str) -> None:
 
 
 def device_metadata(cache, device: torch.device, extra: list[list[int]] | None = None):
-    """Uploads the block table and sequence lengths of ``cache`` (plus any
-    ``extra`` int32 rows) with one pinned host->device copy.
-
-    Returns ``(page_table[B, max_pages], seq_lens[B], extras..., max_pages)``
-    as int32 device tensors.  Works on the reference's own cache objects as
-    well as on this module's: only ``states[i].block_ids`` / ``seq_len`` are
-    read.
-    """
-    states = cache.states
-    B = len(states)
-    max_pages = max((len(s.block_ids) for s in states), default=0)
-    rows = 1 + (len(extra) if extra else 0)
-    n = B * max_pages + B * rows
-    host = np.empty(n, dtype=np.int32)
-    if max_pages:
-        table = host[: B * max_pages].reshape(B, max_pages)
-        table.fill(-1)
-        for r, s in enumerate(states):
-            ids = s.block_ids
-            if ids:
-                table[r, : len(ids)] = ids
-    o = B * max_pages
-    host[o:o + B] = [s.seq_len for s in states]
-    if extra:
-        for i, row in enumerate(extra):
-            host[o + B * (i + 1): o + B * (i + 2)] = row
-    dev = stage_int32(host, device)
-    page_table = dev[: B * max_pages].view(B, max_pages)
-    outs = [page_table]
-    for i in range(rows):
-        outs.append(dev[o + B * i: o + B * (i + 1)])
-    outs.append(max_pages)
-    return tuple(outs)
+    """Block table and sequence lengths of ``cache`` (plus any ``extra`` int32
+    rows) on the device: ``(page_table[B, width], seq_lens[B], extras...,
+    max_pages)``.  The table is cached per batch and patched incrementally
+    (see ``_metadata``).  Works on the reference's own cache objects as well as
+    on this module's: only ``states[i].block_ids`` / ``seq_len`` are read."""
+    return block_table_and_lengths(cache, device, extra)
 
 
 def _kv_append(cache, k_new: torch.Tensor, v_new: torch.Tensor, starts: list[int], lengths: list[int]) -> None:
@@ -318,15 +293,16 @@ def _kv_append(cache, k_new: torch.Tensor, v_new: torch.Tensor, starts: list[int
         raise ValueError(f"pool on {kb.device} but k_new on {k_new.device}")
     B, H, T, D = k_new.shape
     dev = k_new.device
-    page_table, _seq, start_t, len_t, max_pages = device_metadata(cache, dev, [starts, lengths])
+    page_table, seq_lens, start_t, len_t, max_pages = device_metadata(cache, dev, [starts, lengths])
     lib = _lib.load()
     rc = lib.b2pa_kv_append(
         k_new.data_ptr(), _lib.strides4(k_new), v_new.data_ptr(), _lib.strides4(v_new),
         kb.data_ptr(), vb.data_ptr(), _lib.strides4(kb), kb.shape[0],
-        page_table.data_ptr() if max_pages else None, max(max_pages, 1), max_pages,
+        page_table.data_ptr() if max_pages else None, page_table.stride(0), max_pages,
         start_t.data_ptr(), len_t.data_ptr(), B, H, T, D, pool.block_size, _lib.dtype_code(k_new.dtype),
         _lib.status_buffer(dev).data_ptr(), _lib.stream_handle(dev))
     _lib.check(rc, "b2pa_kv_append")
+    return seq_lens
 
 
 def _zero_blocks(pool: LayerBlockPool, block_ids: list[int]) -> None:

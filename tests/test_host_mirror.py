@@ -134,3 +134,27 @@ def test_memory_accounting_matches_reference_formulas():
     assert st.live_bytes() == 20 * 8 * 64 * 2 * es
     assert st.reserved_bytes() == 2 * pool.bytes_per_block()
     assert st.fragmentation_bytes() == st.reserved_bytes() - st.live_bytes()
+
+
+def test_incremental_block_table_matches_full_rebuild():
+    """The cached host table (b2pa._metadata) patched row by row equals a full
+    rebuild after appends across block boundaries, releases and re-appends."""
+    from b2pa import _metadata
+
+    rng = np.random.default_rng(3)
+    pool = b2pa.LayerBlockPool(block_size=16, initial_blocks=4, growth_factor=2.0)
+    states = [b2pa.PagedKVCacheState(pool=pool) for _ in range(9)]
+    cache = b2pa.BatchedPagedKVCache(states, pool=pool)
+    ent = None
+    for step in range(40):
+        lens = rng.integers(0, 40, size=9).tolist()
+        cache.append_batch(_meta(9, 1, 40, 16), _meta(9, 1, 40, 16), lens)
+        if step % 7 == 3:
+            states[step % 9].release()
+        full = cache.page_table_array()
+        if ent is None or full.shape[1] > ent.width:
+            ent = _metadata._Entry(states, max(full.shape[1], 1) * 2)
+        _metadata._refresh_rows(ent)
+        w = full.shape[1]
+        assert np.array_equal(ent.table[:, :w], full)
+        assert (ent.table[:, w:] == -1).all()
