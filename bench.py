@@ -57,6 +57,9 @@ def parse_args(argv=None):
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default: --steps)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU work of the baseline sample")
+    ap.add_argument("--workload", choices=["decode", "prefill", "decode_f32"], default="decode",
+                    help="decode: config[4] (default, the headline); prefill: config[2] chunked prefill "
+                         "(bf16 and fp32); decode_f32: config[1]")
     return ap.parse_args(argv)
 
 
@@ -296,6 +299,8 @@ def main(argv=None) -> int:
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         return main_reference(args, rank, world)
+    if args.workload != "decode":
+        return main_secondary(args)
 
     import torch
     import torch.distributed as dist
@@ -446,6 +451,127 @@ def main(argv=None) -> int:
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(result))
+    return 0
+
+
+# ------------------------------------------------------ secondary workloads
+def _prefill_flops(prefix: np.ndarray, T: int, H: int, D: int) -> float:
+    """4*H*D flops per (query row, visible key): row t of a chunk over a
+    prefix P sees P + t + 1 keys."""
+    return float(4 * H * D * np.sum(T * prefix + T * (T + 1) // 2))
+
+
+def main_secondary(args) -> int:
+    """Kernel-level measurements of BASELINE config[2] (chunked prefill, bf16
+    and fp32) and config[1] (fp32 decode + append) through the C ABI with
+    device-resident inputs; one JSON line per dtype."""
+    import torch
+
+    from b2pa import _lib
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lib = _lib.load()
+    status = _lib.status_buffer(dev).data_ptr()
+    peaks = _peaks()
+    rng = np.random.default_rng(2 if args.workload == "prefill" else 1)
+    Hs, Ds, NB, bs = 8, 64, 4096, 16
+    B = 8 if args.workload == "prefill" else 64
+    T = 256 if args.workload == "prefill" else 1
+    if args.workload == "prefill":
+        prefix = rng.integers(0, 769, size=B)
+    else:
+        prefix = rng.integers(128, 1025, size=B)  # context before this step's token
+    lens = prefix + T
+    pages = (lens + bs - 1) // bs
+    perm = rng.permutation(NB).astype(np.int32)
+    max_pages = int(pages.max())
+    table = np.full((B, max_pages), -1, dtype=np.int32)
+    o = 0
+    for b in range(B):
+        table[b, :pages[b]] = perm[o:o + pages[b]]
+        o += int(pages[b])
+    dtypes = [torch.bfloat16, torch.float32] if args.workload == "prefill" else [torch.float32]
+    lines = []
+    for dtype in dtypes:
+        gen = torch.Generator(device=dev).manual_seed(7)
+        kp = torch.randn(NB, Hs, bs, Ds, generator=gen, device=dev).to(dtype)
+        vp = torch.randn_like(kp)
+        x = torch.randn(B, T, 3, Hs, Ds, generator=gen, device=dev).to(dtype)
+        kn, vn, q = (x[:, :, i].transpose(1, 2) for i in range(3))
+        out = torch.empty_like(q)
+        pt = torch.from_numpy(table).to(dev)
+        start = torch.from_numpy(prefix.astype(np.int32)).to(dev)
+        seq = torch.from_numpy(lens.astype(np.int32)).to(dev)
+        cur = torch.full((B,), T, dtype=torch.int32, device=dev)
+        dt = _lib.dtype_code(dtype)
+        sh = torch.cuda.current_stream(dev).cuda_stream
+        scale = 1.0 / math.sqrt(Ds)
+        ws_n = lib.b2pa_paged_decode_workspace_size(B, Hs, Ds, max_pages, bs, dt) if T == 1 else 0
+        ws = _lib.workspace(dev, max(ws_n, 1))
+
+        def append():
+            _lib.check(lib.b2pa_kv_append(kn.data_ptr(), _lib.strides4(kn), vn.data_ptr(), _lib.strides4(vn),
+                                          kp.data_ptr(), vp.data_ptr(), _lib.strides4(kp), NB, pt.data_ptr(),
+                                          max_pages, max_pages, start.data_ptr(), cur.data_ptr(), B, Hs, T, Ds,
+                                          bs, dt, status, sh), "append")
+
+        def attend():
+            if T == 1:
+                rc = lib.b2pa_paged_decode(q.data_ptr(), _lib.strides4(q), kp.data_ptr(), vp.data_ptr(),
+                                           _lib.strides4(kp), NB, pt.data_ptr(), max_pages, max_pages,
+                                           seq.data_ptr(), cur.data_ptr(), out.data_ptr(), _lib.strides4(out),
+                                           B, Hs, Ds, bs, scale, dt, ws.data_ptr(), ws.numel(), status, sh)
+            else:
+                rc = lib.b2pa_paged_prefill(q.data_ptr(), _lib.strides4(q), kp.data_ptr(), vp.data_ptr(),
+                                            _lib.strides4(kp), NB, pt.data_ptr(), max_pages, max_pages,
+                                            seq.data_ptr(), cur.data_ptr(), out.data_ptr(), _lib.strides4(out),
+                                            B, Hs, T, Ds, bs, scale, dt, None, 0, status, sh)
+            _lib.check(rc, "attention")
+
+        for _ in range(max(args.warmup, 3)):
+            append()
+            attend()
+        torch.cuda.synchronize()
+        # L2 flush buffer (the config[2]/[1] working sets fit in the 126 MB L2)
+        flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+               torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for e0, e1, e2 in ev:
+            flush.zero_()
+            e0.record()
+            append()
+            e1.record()
+            attend()
+            e2.record()
+        torch.cuda.synchronize()
+        _lib.raise_on_device_status(dev, "secondary bench")
+        step_ms = float(np.mean([a.elapsed_time(c) for a, _, c in ev]))
+        attn_ms = float(np.mean([b.elapsed_time(c) for _, b, c in ev]))
+        es = 2 if dtype == torch.bfloat16 else 4
+        kv_bytes = 2 * Hs * Ds * es * int(lens.sum())
+        line = {"workload": args.workload, "dtype": str(dtype).replace("torch.", ""), "steps": args.steps,
+                "config": {"B": B, "H": Hs, "D": Ds, "T": T, "block_size": bs, "pool_blocks": NB,
+                           "l2": "flushed (256 MB write) before every step"},
+                "ms_per_step_append_plus_attention": step_ms, "attention_ms": attn_ms,
+                "append_ms": step_ms - attn_ms}
+        if T > 1:
+            flops = _prefill_flops(prefix, T, Hs, Ds)
+            bytes_ = kv_bytes + 2 * B * Hs * T * Ds * es
+            line.update({"tokens_per_s": B * T / (step_ms / 1e3), "attention_tflops": flops / (attn_ms / 1e3) / 1e12,
+                         "flops_per_launch": flops, "bytes_per_launch": bytes_,
+                         "attention_hbm_gbs": bytes_ / (attn_ms / 1e3) / 1e9,
+                         "frac_of_bf16_tensor_peak": flops / (attn_ms / 1e3) / 1e12 / peaks["bf16_tflops"],
+                         "frac_of_hbm_peak": bytes_ / (attn_ms / 1e3) / 1e9 / peaks["hbm_gbs"]})
+        else:
+            bytes_ = kv_bytes + 2 * B * Hs * Ds * es + 4 * int(pages.sum()) + 8 * B
+            line.update({"tokens_per_s": B / (step_ms / 1e3), "attention_hbm_gbs": bytes_ / (attn_ms / 1e3) / 1e9,
+                         "bytes_per_launch": bytes_,
+                         "frac_of_hbm_peak": bytes_ / (attn_ms / 1e3) / 1e9 / peaks["hbm_gbs"]})
+        lines.append(line)
+        print(json.dumps(line))
+        del kp, vp, flush
+        torch.cuda.empty_cache()
     return 0
 
 

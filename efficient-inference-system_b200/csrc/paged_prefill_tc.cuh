@@ -1,0 +1,392 @@
+// paged_prefill_tc.cuh -- chunked-prefill paged attention on the 5th-gen
+// tensor cores (tcgen05 + TMEM), bf16/fp16 inputs, fp32 accumulation.
+//
+// Replaces the Triton prefill kernel of the reference
+// (src/kernels/triton_paged_attention.py:88-176, launcher :220-258) for
+// 16-bit pools with head_dim 64 or 128; semantics as in
+// src/kernels/reference_paged_attention.py:31-57 (query row t of sequence b
+// sees keys 0 .. min(seq_len, seq_len - cur_len + t + 1) - 1; rows that see
+// nothing are zero; rows past cur_len see the whole sequence).
+//
+// One CTA = (128 query rows, head, sequence); 6 warps:
+//   warp 4  producer: per 64-key tile, one TMA tensor load per page and
+//           128-byte column block for K and for V (block table gather; the
+//           pool is viewed as a 2-d [blocks*H*block_size, D] tensor with a
+//           128B-swizzle map), into a 2-stage ring;
+//   warp 5  MMA issuer (one elected lane): S = Q.K^T (M=128, N=64, K=D) into
+//           TMEM, then O_tile = P.V (M=128, N=D, K=64) into TMEM; completion
+//           signalled with tcgen05.commit on mbarriers;
+//   warps 0-3 softmax: thread r owns query row r: reads its S row from TMEM,
+//           masks, online softmax in the log2 domain, writes P (bf16/fp16,
+//           128B-swizzled K-major) to shared memory for the next MMA, and
+//           accumulates O_tile from TMEM into fp32 registers with the
+//           running rescale.  The output is divided by max(l, 1e-9).
+// Q is loaded by the softmax threads (arbitrary strides) into the swizzled
+// layout.  Every mbarrier wait is bounded (1 s); a wait that gives up records
+// B2PA_ERR_DEVICE_TIMEOUT, raises a CTA-wide abort flag and the roles drain
+// to the final barrier so TMEM is always freed.  No multicast anywhere.
+#pragma once
+
+#include <cuda.h>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tcgen05.cuh"
+
+namespace b2pa {
+
+struct PfTcParams {
+  const void* q;
+  int64_t sq_b, sq_h, sq_t;
+  const int32_t* page_table;
+  int64_t pt_stride;
+  int max_pages;
+  const int32_t* seq_lens;
+  const int32_t* cur_lens;
+  void* out;
+  int64_t so_b, so_h, so_t;
+  int B, H, T;
+  int64_t num_blocks;
+  float scale_log2;
+  int32_t* status;
+};
+
+template <int D, int BS>
+struct PfTcCfg {
+  static constexpr int BM = 128;         // query rows per CTA (UMMA M)
+  static constexpr int BN = 64;          // keys per tile
+  static constexpr int KB = D / 64;      // 128-byte column blocks of a row
+  static constexpr int PAGES = BN / BS;  // pages per key tile
+  static constexpr int STAGES = 2;
+  static constexpr int Q_BYTES = BM * D * 2;
+  static constexpr int KV_BYTES = BN * D * 2;
+  static constexpr int P_BYTES = BM * BN * 2;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_K = OFF_Q + Q_BYTES;
+  static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
+  static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
+  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  static constexpr int N_BARS = 2 * STAGES + 3;
+  static constexpr int OFF_MISC = OFF_BAR + 8 * N_BARS;
+  static constexpr int SMEM = OFF_MISC + 16 + 1024;  // + alignment slack
+  static constexpr int TMEM_COLS = (BN + D) <= 128 ? 128 : 256;
+  static constexpr int THREADS = 192;
+  static_assert(D == 64 || D == 128, "tcgen05 prefill is built for head_dim 64 and 128");
+  static_assert(BN % BS == 0, "block size must divide the key tile");
+};
+
+// Waits with every lane of the warp; false (for all lanes) if any gave up.
+__device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int32_t* status, volatile int* abort_flag) {
+  if (*abort_flag) return false;
+  const bool ok = __all_sync(kFullMask, mbar_wait_bounded(bar, parity, status));
+  if (!ok) *abort_flag = 1;
+  return ok;
+}
+
+template <typename T, int D, int BS>
+__global__ void __launch_bounds__(192, 1)
+    paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
+                            PfTcParams p) {
+  using C = PfTcCfg<D, BS>;
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sQ = smem + C::OFF_Q;
+  unsigned char* sK = smem + C::OFF_K;
+  unsigned char* sV = smem + C::OFF_V;
+  unsigned char* sP = smem + C::OFF_P;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* kv_full = bars;
+  uint64_t* kv_empty = bars + C::STAGES;
+  uint64_t* s_full = bars + 2 * C::STAGES;
+  uint64_t* p_full = s_full + 1;
+  uint64_t* o_full = s_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t0 = blockIdx.x * C::BM;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+
+  const int64_t L = p.seq_lens[b];
+  const int64_t past = L - (int64_t)p.cur_lens[b];
+  const int64_t cap = (int64_t)p.max_pages * BS;
+  const int t_last = (t0 + C::BM < p.T ? t0 + C::BM : p.T) - 1;
+  int64_t kend = L < past + t_last + 1 ? L : past + t_last + 1;
+  if (kend > cap) kend = cap;
+  if (kend < 0) kend = 0;
+  const int ntiles = (int)((kend + C::BN - 1) / C::BN);
+
+  if (tid == 0) {
+    if (L > cap) set_status(p.status, B2PA_ERR_BAD_BLOCK_ID);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 4);
+    mbar_init(o_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 5) {
+    tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tc::tmem_relinquish();
+  }
+  if (warp == 4 && lane == 0) {
+    tc::prefetch_tmap(&tm_k);
+    tc::prefetch_tmap(&tm_v);
+  }
+  if (warp < 4) {
+    // Q rows -> 128B-swizzled K-major tile, zeros past T.
+    const int r = tid;
+    const int t = t0 + r;
+    const T* qrow = static_cast<const T*>(p.q) + (int64_t)b * p.sq_b + (int64_t)h * p.sq_h + (int64_t)t * p.sq_t;
+#pragma unroll
+    for (int c = 0; c < D / 8; ++c) {
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (t < p.T) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
+      *reinterpret_cast<uint4*>(sQ + (c >> 3) * (C::BM * 128) + tc::sw128_offset(r, c & 7)) = v;
+    }
+    tc::fence_proxy_async_smem();
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  tc::fence_after_sync();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS = tmem;           // columns [0, 64): S
+  const uint32_t tO = tmem + C::BN;   // columns [64, 64 + D): O tile
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j % C::STAGES;
+      const uint32_t ph = (uint32_t)(j / C::STAGES) & 1u;
+      if (!warp_wait(&kv_empty[st], ph ^ 1u, p.status, abort_flag)) break;
+      int blks[C::PAGES];
+      uint32_t bytes = 0;
+#pragma unroll
+      for (int pg = 0; pg < C::PAGES; ++pg) {
+        const int64_t page = (int64_t)j * C::PAGES + pg;
+        int blk = -1;
+        if (page * BS < kend) {
+          blk = p.page_table[(int64_t)b * p.pt_stride + page];
+          if (blk >= p.num_blocks) {
+            if (lane == 0) set_status(p.status, B2PA_ERR_BAD_BLOCK_ID);
+            blk = -1;
+          }
+        }
+        blks[pg] = blk;
+        if (blk >= 0) {
+          bytes += 2u * BS * D * 2;
+        } else {
+          // Pages that are not loaded must not hold stale or uninitialised
+          // bytes: their softmax weight is 0, but 0 * NaN is NaN in P.V.
+#pragma unroll
+          for (int kb = 0; kb < C::KB; ++kb) {
+            const int off = st * C::KV_BYTES + kb * (C::BN * 128) + pg * (BS * 128);
+            for (int i = lane; i < BS * 8; i += 32) {
+              reinterpret_cast<uint4*>(sK + off)[i] = make_uint4(0, 0, 0, 0);
+              reinterpret_cast<uint4*>(sV + off)[i] = make_uint4(0, 0, 0, 0);
+            }
+          }
+        }
+      }
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&kv_full[st], bytes);
+#pragma unroll
+        for (int pg = 0; pg < C::PAGES; ++pg) {
+          if (blks[pg] < 0) continue;
+          const int row = (blks[pg] * p.H + h) * BS;
+#pragma unroll
+          for (int kb = 0; kb < C::KB; ++kb) {
+            const int off = st * C::KV_BYTES + kb * (C::BN * 128) + pg * (BS * 128);
+            tc::tma_load_2d(sK + off, &tm_k, kb * 64, row, &kv_full[st]);
+            tc::tma_load_2d(sV + off, &tm_v, kb * 64, row, &kv_full[st]);
+          }
+        }
+      }
+      __syncwarp();
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issue
+    constexpr int FMT = sizeof(T) == 2 && ElemTraits<T>::kDtype == B2PA_DTYPE_BF16 ? 1 : 0;
+    constexpr uint32_t idesc_s = tc::idesc_f16(128, C::BN, FMT, 0, 0);
+    constexpr uint32_t idesc_o = tc::idesc_f16(128, D, FMT, 0, 1);
+    const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
+    for (int j = 0; j < ntiles; ++j) {
+      const int st = j % C::STAGES;
+      const uint32_t ph = (uint32_t)(j / C::STAGES) & 1u;
+      if (!warp_wait(&kv_full[st], ph, p.status, abort_flag)) break;
+      tc::fence_after_sync();
+      if (lane == 0) {
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          const int kb = k >> 2, kk = k & 3;
+          const uint64_t a = tc::smem_desc(aQ + kb * (C::BM * 128) + kk * 32, 16, 1024);
+          const uint64_t bd = tc::smem_desc(aK + st * C::KV_BYTES + kb * (C::BN * 128) + kk * 32, 16, 1024);
+          tc::mma_f16_ss(tS, a, bd, idesc_s, k > 0);
+        }
+        tc::commit(s_full);
+      }
+      __syncwarp();
+      if (!warp_wait(p_full, (uint32_t)j & 1u, p.status, abort_flag)) break;
+      tc::fence_after_sync();
+      if (lane == 0) {
+#pragma unroll
+        for (int k = 0; k < C::BN / 16; ++k) {
+          const uint64_t a = tc::smem_desc(aP + k * 32, 16, 1024);
+          const uint64_t bd = tc::smem_desc(aV + st * C::KV_BYTES + k * 2048, C::BN * 128, 1024);
+          tc::mma_f16_ss(tO, a, bd, idesc_o, k > 0);
+        }
+        tc::commit(o_full);
+        tc::commit(&kv_empty[st]);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------ softmax
+    const int r = tid;
+    const int t = t0 + r;
+    int64_t row_end = L < past + t + 1 ? L : past + t + 1;
+    if (row_end > cap) row_end = cap;
+    const uint32_t trow = (uint32_t)(warp * 32) << 16;
+    float o[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) o[i] = 0.f;
+    float m = -INFINITY, l = 0.f;
+    for (int j = 0; j < ntiles; ++j) {
+      if (!warp_wait(s_full, (uint32_t)j & 1u, p.status, abort_flag)) break;
+      tc::fence_after_sync();
+      float s[64];
+      {
+        float a[32], c[32];
+        tc::tmem_ld32(tS + trow, a);
+        tc::tmem_ld32(tS + trow + 32, c);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          s[i] = a[i];
+          s[32 + i] = c[i];
+        }
+      }
+      const int64_t k0 = (int64_t)j * C::BN;
+      bool page_ok[C::PAGES];
+#pragma unroll
+      for (int pg = 0; pg < C::PAGES; ++pg) {
+        const int64_t page = k0 / BS + pg;
+        bool ok = false;
+        if (page * BS < kend) {
+          const int blk = p.page_table[(int64_t)b * p.pt_stride + page];
+          ok = blk >= 0 && blk < p.num_blocks;
+        }
+        page_ok[pg] = ok;
+      }
+      float mt = -INFINITY;
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const bool vis = (k0 + i < row_end) && page_ok[i / BS];
+        s[i] = vis ? s[i] * p.scale_log2 : -INFINITY;
+        mt = fmaxf(mt, s[i]);
+      }
+      const float m_new = fmaxf(m, mt);
+      const bool live = m_new != -INFINITY;
+      const float alpha = live ? exp2f(m - m_new) : 1.f;
+      float lsum = 0.f;
+#pragma unroll
+      for (int c8 = 0; c8 < 8; ++c8) {
+        float pv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          pv[e] = live ? exp2f(s[c8 * 8 + e] - m_new) : 0.f;
+          lsum += pv[e];
+        }
+        Vec<T, 8> w;
+        w.from_float(pv);
+        *reinterpret_cast<uint4*>(sP + tc::sw128_offset(r, c8)) = w.w;
+      }
+      l = l * alpha + lsum;
+      m = m_new;
+      tc::fence_proxy_async_smem();
+      tc::fence_before_sync();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      if (!warp_wait(o_full, (uint32_t)j & 1u, p.status, abort_flag)) break;
+      tc::fence_after_sync();
+#pragma unroll
+      for (int cb = 0; cb < D / 32; ++cb) {
+        float ot[32];
+        tc::tmem_ld32(tO + trow + cb * 32, ot);
+        tc::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[cb * 32 + i] = fmaf(o[cb * 32 + i], alpha, ot[i]);
+      }
+      tc::fence_before_sync();
+    }
+    if (t < p.T) {
+      const float den = fmaxf(l, 1e-9f);
+      T* orow = static_cast<T*>(p.out) + (int64_t)b * p.so_b + (int64_t)h * p.so_h + (int64_t)t * p.so_t;
+#pragma unroll
+      for (int c8 = 0; c8 < D / 8; ++c8) {
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = o[c8 * 8 + e] / den;
+        Vec<T, 8> w;
+        w.from_float(f);
+        *reinterpret_cast<uint4*>(orow + c8 * 8) = w.w;
+      }
+    }
+  }
+  tc::fence_before_sync();
+  __syncthreads();
+  if (warp == 5) {
+    tc::fence_after_sync();
+    tc::tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ----------------------------------------------------------------- host ---
+bool encode_pool_tensor_map(CUtensorMap* map, const void* pool, int64_t rows, int D, int block_size, int dtype);
+
+template <typename T, int D, int BS>
+int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream) {
+  using C = PfTcCfg<D, BS>;
+  CUtensorMap tmk, tmv;
+  const int64_t rows = a.num_blocks * a.H * BS;
+  if (!encode_pool_tensor_map(&tmk, a.k_pool, rows, D, BS, a.dtype) ||
+      !encode_pool_tensor_map(&tmv, a.v_pool, rows, D, BS, a.dtype))
+    return set_error(B2PA_ERR_CUDA, "paged_prefill: cuTensorMapEncodeTiled failed for the pools");
+  PfTcParams p;
+  p.q = a.q;
+  p.sq_b = a.sq[0];
+  p.sq_h = a.sq[1];
+  p.sq_t = a.sq[2];
+  p.page_table = a.page_table;
+  p.pt_stride = a.pt_stride;
+  p.max_pages = a.max_pages;
+  p.seq_lens = a.seq_lens;
+  p.cur_lens = a.cur_lens;
+  p.out = a.out;
+  p.so_b = a.so[0];
+  p.so_h = a.so[1];
+  p.so_t = a.so[2];
+  p.B = a.B;
+  p.H = a.H;
+  p.T = a.T;
+  p.num_blocks = a.num_blocks;
+  p.scale_log2 = a.scale * kLog2e;
+  p.status = a.status;
+  auto kern = paged_prefill_tc_kernel<T, D, BS>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill_tc smem attribute: %s", cudaGetErrorString(e));
+  dim3 grid((a.T + C::BM - 1) / C::BM, a.H, a.B);
+  kern<<<grid, C::THREADS, C::SMEM, stream>>>(tmk, tmv, p);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill_tc launch: %s", cudaGetErrorString(e));
+  return B2PA_OK;
+}
+
+}  // namespace b2pa

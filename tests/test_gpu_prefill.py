@@ -97,3 +97,26 @@ def test_prefill_through_append(cuda_device):
                                     [s.seq_len for s in mstates], lens)
         _check(out, ref, torch.float32)
     assert b2pa.read_status(cuda_device) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("D", [64, 128])
+def test_prefill_tensor_core_multi_tile(cuda_device, dtype, D):
+    # several 128-row query tiles, long prefixes, chunk rows padded at the end
+    out, ref = _random_prefill(cuda_device, B=3, H=2, D=D, bs=16, T=300, dtype=dtype, prefixes=[0, 500, 1000],
+                               curs=[300, 171, 300], seed=D)
+    _check(out, ref, dtype)
+    assert b2pa.read_status(cuda_device) == 0
+
+
+def test_prefill_bad_block_id_is_reported(cuda_device):
+    torch.manual_seed(1)
+    kp = torch.randn(4, 2, 16, 64, device=cuda_device, dtype=torch.bfloat16)
+    vp = torch.randn_like(kp)
+    cache = build_cache(b2pa, kp, vp, [[0, 9, 1]], [40], 16)  # block 9 is past the pool
+    b2pa.clear_status(cuda_device)
+    q = torch.randn(1, 2, 20, 64, device=cuda_device, dtype=torch.bfloat16)
+    out = b2pa.paged_attention("b200_paged", q, cache, 20)
+    assert b2pa.read_status(cuda_device) == -3
+    b2pa.clear_status(cuda_device)
+    assert torch.isfinite(out.float()).all()
