@@ -84,6 +84,19 @@ def algorithmic_decode_bytes(lens_post: np.ndarray, es: int = 2) -> int:
     return int(2 * H * D * es * int(lens_post.sum()) + 2 * B * H * D * es + 4 * pages + 8 * B)
 
 
+def max_over_ranks(values: list[float], device, world: int) -> list[float]:
+    """Element-wise max of per-rank timings (all ranks call it, in the same
+    order); identity on one rank."""
+    if world == 1:
+        return list(values)
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.tolist()
+
+
 class Workload:
     """This rank's pool, block tables and per-step metadata, on the device."""
 
@@ -384,10 +397,7 @@ def main(argv=None) -> int:
     _lib.raise_on_device_status(dev, "e2e steps")
 
     # ------------------------------------------------------ aggregate
-    times = torch.tensor([elapsed_ms, e2e_ms, float(np.mean(decode_ms))], dtype=torch.float64, device=dev)
-    if world > 1:
-        dist.all_reduce(times, op=dist.ReduceOp.MAX)
-    elapsed_ms, e2e_ms, decode_avg_ms = times.tolist()
+    elapsed_ms, e2e_ms, decode_avg_ms = max_over_ranks([elapsed_ms, e2e_ms, float(np.mean(decode_ms))], dev, world)
     total_seqs = B * world
     value = total_seqs * args.steps / (elapsed_ms / 1e3)
     e2e_value = total_seqs * e2e_steps / (e2e_ms / 1e3)

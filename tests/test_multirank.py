@@ -1,0 +1,59 @@
+"""Host-side logic of the multi-GPU bench path on CPU with the gloo backend
+(world size 2): every sequence is owned by exactly one rank, weak scaling
+gives each rank the same count, and timings reduce to the max over ranks."""
+from __future__ import annotations
+
+import os
+import socket
+from types import SimpleNamespace
+
+import numpy as np
+import pytest
+import torch.multiprocessing as mp
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    import bench
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        for scaling in ("strong", "weak"):
+            args = SimpleNamespace(scaling=scaling, seqs=37)
+            mine = bench.my_sequences(args, rank, world)
+            got = [None] * world
+            dist.all_gather_object(got, mine.tolist())
+            if rank == 0:
+                np.save(os.path.join(out_dir, f"{scaling}.npy"), np.array(got, dtype=object), allow_pickle=True)
+        t = bench.max_over_ranks([1.0 + rank, 5.0 - rank], torch.device("cpu"), world)
+        if rank == 0:
+            np.save(os.path.join(out_dir, "max.npy"), np.array(t))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_partition_and_max_reduction(tmp_path):
+    import bench
+
+    world = 2
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    strong = np.load(tmp_path / "strong.npy", allow_pickle=True)
+    full = bench.all_lengths(37).tolist()
+    merged = sorted(x for part in strong for x in part)
+    assert merged == sorted(full)                       # strong: one shared set, split
+    assert abs(len(strong[0]) - len(strong[1])) <= 1
+    weak = np.load(tmp_path / "weak.npy", allow_pickle=True)
+    assert len(weak[0]) == len(weak[1]) == 37           # weak: 37 per rank
+    assert sorted(x for p in weak for x in p) == sorted(bench.all_lengths(74).tolist())
+    assert np.load(tmp_path / "max.npy").tolist() == [2.0, 5.0]
