@@ -517,7 +517,8 @@ def main_secondary(args) -> int:
         dt = _lib.dtype_code(dtype)
         sh = torch.cuda.current_stream(dev).cuda_stream
         scale = 1.0 / math.sqrt(Ds)
-        ws_n = lib.b2pa_paged_decode_workspace_size(B, Hs, Ds, max_pages, bs, dt) if T == 1 else 0
+        ws_n = (lib.b2pa_paged_decode_workspace_size(B, Hs, Ds, max_pages, bs, dt) if T == 1 else
+                lib.b2pa_paged_prefill_workspace_size(B, Hs, T, Ds, max_pages, bs, dt))
         ws = _lib.workspace(dev, max(ws_n, 1))
 
         def append():
@@ -536,7 +537,7 @@ def main_secondary(args) -> int:
                 rc = lib.b2pa_paged_prefill(q.data_ptr(), _lib.strides4(q), kp.data_ptr(), vp.data_ptr(),
                                             _lib.strides4(kp), NB, pt.data_ptr(), max_pages, max_pages,
                                             seq.data_ptr(), cur.data_ptr(), out.data_ptr(), _lib.strides4(out),
-                                            B, Hs, T, Ds, bs, scale, dt, None, 0, status, sh)
+                                            B, Hs, T, Ds, bs, scale, dt, ws.data_ptr(), ws.numel(), status, sh)
             _lib.check(rc, "attention")
 
         for _ in range(max(args.warmup, 3)):

@@ -122,6 +122,40 @@ DecodePlan make_decode_plan(int B, int H, int D, int max_pages, int block_size, 
   return pl;
 }
 
+bool prefill_uses_tensor_cores(int D, int block_size, int dtype, int64_t pool_rows) {
+  return (dtype == B2PA_DTYPE_BF16 || dtype == B2PA_DTYPE_F16) && (D == 64 || D == 128) &&
+         (block_size == 8 || block_size == 16 || block_size == 32) && pool_rows <= ((int64_t)1 << 31);
+}
+
+// Split the key range of the tensor-core prefill when the (query tile, head,
+// sequence) CTAs alone would leave most of the machine idle.  The kernel runs
+// one CTA per SM, so the split CTAs must still fit in one wave of a 148-SM
+// part (extra waves cost more than the shorter key walks save); at least 2
+// key tiles per CTA.
+PrefillPlan make_prefill_plan(int B, int H, int T, int D, int max_pages, int block_size, int dtype) {
+  PrefillPlan pl;
+  const int64_t ktmax = ((int64_t)max_pages * block_size + 63) / 64;
+  pl.kt_per_split = (int)(ktmax > 0 ? ktmax : 1);
+  pl.nsplit_max = 1;
+  pl.off_part_ml = pl.off_part_o = pl.bytes = 0;
+  if (!prefill_uses_tensor_cores(D, block_size, dtype, 0) || B <= 0 || T <= 0 || ktmax <= 2) return pl;
+  const int64_t ctas = (int64_t)B * H * ((T + 127) / 128);
+  int64_t splits = 148 / ctas;
+  if (splits > ktmax) splits = ktmax;
+  if (splits <= 1) return pl;
+  int64_t kt = (ktmax + splits - 1) / splits;
+  if (kt < 2) kt = 2;
+  const int64_t ns = (ktmax + kt - 1) / kt;
+  if (ns <= 1) return pl;
+  pl.kt_per_split = (int)kt;
+  pl.nsplit_max = (int)ns;
+  const size_t slots = (size_t)B * H * T * ns;
+  pl.off_part_ml = 0;
+  pl.off_part_o = align_up(8 * slots, 256);
+  pl.bytes = align_up(pl.off_part_o + 4 * slots * D, 256);
+  return pl;
+}
+
 }  // namespace b2pa
 
 using namespace b2pa;
@@ -300,8 +334,8 @@ int b2pa_paged_decode(const void* q, const int64_t q_strides[4], const void* k_p
 }
 
 size_t b2pa_paged_prefill_workspace_size(int B, int H, int T, int D, int max_pages, int block_size, int dtype) {
-  (void)B; (void)H; (void)T; (void)D; (void)max_pages; (void)block_size; (void)dtype;
-  return 0;
+  if (B <= 0 || H <= 0 || T <= 0 || D <= 0 || max_pages < 0 || block_size <= 0 || dtype_size(dtype) == 0) return 0;
+  return make_prefill_plan(B, H, T, D, max_pages, block_size, dtype).bytes;
 }
 
 int b2pa_paged_prefill(const void* q, const int64_t q_strides[4], const void* k_pool, const void* v_pool,

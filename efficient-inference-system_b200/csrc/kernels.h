@@ -86,6 +86,16 @@ int launch_paged_decode_f32(const AttnArgs& a, const DecodePlan& plan, cudaStrea
 int launch_paged_decode_bf16(const AttnArgs& a, const DecodePlan& plan, cudaStream_t s);
 int launch_paged_decode_f16(const AttnArgs& a, const DecodePlan& plan, cudaStream_t s);
 
+// Key-range split of the tensor-core prefill (shared by the workspace query
+// and the launcher).  bytes == 0 means no split and no workspace.
+struct PrefillPlan {
+  int kt_per_split;  // 64-key tiles per CTA
+  int nsplit_max;
+  size_t off_part_ml, off_part_o, bytes;
+};
+PrefillPlan make_prefill_plan(int B, int H, int T, int D, int max_pages, int block_size, int dtype);
+bool prefill_uses_tensor_cores(int D, int block_size, int dtype, int64_t pool_rows);
+
 int launch_paged_prefill_f32(const AttnArgs& a, cudaStream_t s);
 int launch_paged_prefill_bf16(const AttnArgs& a, cudaStream_t s);
 int launch_paged_prefill_f16(const AttnArgs& a, cudaStream_t s);

@@ -5,8 +5,7 @@
 
 namespace b2pa {
 int launch_paged_prefill_bf16(const AttnArgs& a, cudaStream_t s) {
-  const bool rows_fit = a.num_blocks * a.H * a.block_size <= ((int64_t)1 << 31);
-  if (rows_fit) {
+  if (prefill_uses_tensor_cores(a.D, a.block_size, a.dtype, a.num_blocks * a.H * a.block_size)) {
 #define B2PA_TC_CASE(DD, BB) \
     if (a.D == DD && a.block_size == BB) return launch_prefill_tc<__nv_bfloat16, DD, BB>(a, s);
     B2PA_TC_CASE(64, 8) B2PA_TC_CASE(64, 16) B2PA_TC_CASE(64, 32)

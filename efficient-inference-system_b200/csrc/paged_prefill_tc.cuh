@@ -49,7 +49,32 @@ struct PfTcParams {
   int64_t num_blocks;
   float scale_log2;
   int32_t* status;
+  // Key-range split: CTA (x = q_tile * nsplit_max + s) covers key tiles
+  // [s*kt_per_split, (s+1)*kt_per_split).  With more than one split the CTAs
+  // write fp32 partials (unnormalised O, running max m, denominator l) that
+  // prefill_combine_kernel merges.
+  int kt_per_split;
+  int nsplit_max;
+  float* part_o;   // [B, H, T, nsplit_max, D]
+  float* part_ml;  // [B, H, T, nsplit_max, 2]
 };
+
+// Key tiles of query tile `t0` of sequence b, and its number of splits.
+__device__ __forceinline__ void prefill_tile_range(const PfTcParams& p, int b, int t0, int bm, int bn, int bs,
+                                                   int64_t* kend_out, int* ntiles_out, int* nsplit_out) {
+  const int64_t L = p.seq_lens[b];
+  const int64_t past = L - (int64_t)p.cur_lens[b];
+  const int64_t cap = (int64_t)p.max_pages * bs;
+  const int t_last = (t0 + bm < p.T ? t0 + bm : p.T) - 1;
+  int64_t kend = L < past + t_last + 1 ? L : past + t_last + 1;
+  if (kend > cap) kend = cap;
+  if (kend < 0) kend = 0;
+  const int ntiles = (int)((kend + bn - 1) / bn);
+  const int ns = (ntiles + p.kt_per_split - 1) / p.kt_per_split;
+  *kend_out = kend;
+  *ntiles_out = ntiles;
+  *nsplit_out = ns < 1 ? 1 : ns;
+}
 
 template <int D, int BS>
 struct PfTcCfg {
@@ -105,18 +130,21 @@ __global__ void __launch_bounds__(192, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int t0 = blockIdx.x * C::BM;
+  const int split = blockIdx.x % p.nsplit_max;
+  const int t0 = (blockIdx.x / p.nsplit_max) * C::BM;
   const int h = blockIdx.y;
   const int b = blockIdx.z;
 
   const int64_t L = p.seq_lens[b];
   const int64_t past = L - (int64_t)p.cur_lens[b];
   const int64_t cap = (int64_t)p.max_pages * BS;
-  const int t_last = (t0 + C::BM < p.T ? t0 + C::BM : p.T) - 1;
-  int64_t kend = L < past + t_last + 1 ? L : past + t_last + 1;
-  if (kend > cap) kend = cap;
-  if (kend < 0) kend = 0;
-  const int ntiles = (int)((kend + C::BN - 1) / C::BN);
+  int64_t kend;
+  int ntiles_all, nsplit;
+  prefill_tile_range(p, b, t0, C::BM, C::BN, BS, &kend, &ntiles_all, &nsplit);
+  if (split >= nsplit) return;  // this query tile needs fewer splits (uniform across the CTA)
+  const int j0 = split * p.kt_per_split;
+  const int j1 = (j0 + p.kt_per_split < ntiles_all) ? j0 + p.kt_per_split : ntiles_all;
+  const int ntiles = j1 > j0 ? j1 - j0 : 0;  // tiles of this CTA; tile index = j0 + local
 
   if (tid == 0) {
     if (L > cap) set_status(p.status, B2PA_ERR_BAD_BLOCK_ID);
@@ -168,7 +196,7 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t bytes = 0;
 #pragma unroll
       for (int pg = 0; pg < C::PAGES; ++pg) {
-        const int64_t page = (int64_t)j * C::PAGES + pg;
+        const int64_t page = (int64_t)(j0 + j) * C::PAGES + pg;
         int blk = -1;
         if (page * BS < kend) {
           blk = p.page_table[(int64_t)b * p.pt_stride + page];
@@ -273,7 +301,7 @@ __global__ void __launch_bounds__(192, 1)
           s[32 + i] = c[i];
         }
       }
-      const int64_t k0 = (int64_t)j * C::BN;
+      const int64_t k0 = (int64_t)(j0 + j) * C::BN;
       bool page_ok[C::PAGES];
 #pragma unroll
       for (int pg = 0; pg < C::PAGES; ++pg) {
@@ -326,7 +354,14 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc::fence_before_sync();
     }
-    if (t < p.T) {
+    if (t < p.T && nsplit > 1) {
+      const int64_t slot = (((int64_t)b * p.H + h) * p.T + t) * p.nsplit_max + split;
+      float4* po = reinterpret_cast<float4*>(p.part_o + slot * D);
+#pragma unroll
+      for (int c4 = 0; c4 < D / 4; ++c4) po[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
+      p.part_ml[2 * slot] = m;
+      p.part_ml[2 * slot + 1] = l;
+    } else if (t < p.T) {
       const float den = fmaxf(l, 1e-9f);
       T* orow = static_cast<T*>(p.out) + (int64_t)b * p.so_b + (int64_t)h * p.so_h + (int64_t)t * p.so_t;
 #pragma unroll
@@ -346,6 +381,42 @@ __global__ void __launch_bounds__(192, 1)
     tc::fence_after_sync();
     tc::tmem_dealloc(tmem, C::TMEM_COLS);
   }
+}
+
+// One warp per (sequence, head, query row) whose query tile was split:
+// log-sum-exp merge of the split partials, then the reference's normalisation.
+template <typename T, int D, int BS>
+__global__ void __launch_bounds__(256) prefill_combine_kernel(PfTcParams p) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * 8 + warp;
+  if (row >= (int64_t)p.B * p.H * p.T) return;
+  const int t = (int)(row % p.T);
+  const int h = (int)((row / p.T) % p.H);
+  const int b = (int)(row / ((int64_t)p.T * p.H));
+  int64_t kend;
+  int ntiles, nsplit;
+  prefill_tile_range(p, b, (t / 128) * 128, 128, 64, BS, &kend, &ntiles, &nsplit);
+  if (nsplit <= 1) return;
+  const int64_t base = row * p.nsplit_max;
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, p.part_ml[2 * (base + s)]);
+  constexpr int PER = D / 32;
+  float o[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) o[i] = 0.f;
+  float L = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const float ms = p.part_ml[2 * (base + s)];
+    const float w = (M == -INFINITY) ? 0.f : exp2f(ms - M);
+    L = fmaf(p.part_ml[2 * (base + s) + 1], w, L);
+    const float* po = p.part_o + (base + s) * D;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) o[i] = fmaf(w, po[lane + 32 * i], o[i]);
+  }
+  const float den = fmaxf(L, 1e-9f);
+  T* orow = static_cast<T*>(p.out) + (int64_t)b * p.so_b + (int64_t)h * p.so_h + (int64_t)t * p.so_t;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) orow[lane + 32 * i] = from_f32<T>(o[i] / den);
 }
 
 // ----------------------------------------------------------------- host ---
@@ -379,11 +450,27 @@ int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream) {
   p.num_blocks = a.num_blocks;
   p.scale_log2 = a.scale * kLog2e;
   p.status = a.status;
+  const PrefillPlan plan = make_prefill_plan(a.B, a.H, a.T, a.D, a.max_pages, BS, a.dtype);
+  p.kt_per_split = plan.kt_per_split;
+  p.nsplit_max = plan.nsplit_max;
+  p.part_o = nullptr;
+  p.part_ml = nullptr;
+  if (plan.bytes > 0) {
+    if (!a.workspace || a.workspace_bytes < plan.bytes)
+      return set_error(B2PA_ERR_WORKSPACE, "paged_prefill: workspace of %zu bytes, %zu needed", a.workspace_bytes,
+                       plan.bytes);
+    p.part_ml = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + plan.off_part_ml);
+    p.part_o = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + plan.off_part_o);
+  }
   auto kern = paged_prefill_tc_kernel<T, D, BS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill_tc smem attribute: %s", cudaGetErrorString(e));
-  dim3 grid((a.T + C::BM - 1) / C::BM, a.H, a.B);
+  dim3 grid(((a.T + C::BM - 1) / C::BM) * plan.nsplit_max, a.H, a.B);
   kern<<<grid, C::THREADS, C::SMEM, stream>>>(tmk, tmv, p);
+  if (plan.nsplit_max > 1) {
+    const int64_t rows = (int64_t)a.B * a.H * a.T;
+    prefill_combine_kernel<T, D, BS><<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(p);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill_tc launch: %s", cudaGetErrorString(e));
   return B2PA_OK;

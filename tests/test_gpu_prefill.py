@@ -120,3 +120,14 @@ def test_prefill_bad_block_id_is_reported(cuda_device):
     assert b2pa.read_status(cuda_device) == -3
     b2pa.clear_status(cuda_device)
     assert torch.isfinite(out.float()).all()
+
+
+@pytest.mark.parametrize("D", [64, 128])
+def test_prefill_tensor_core_key_split(cuda_device, D):
+    # few (query tile, head, sequence) CTAs: the key range is split across
+    # CTAs and merged by the combine kernel; the second sequence is short, so
+    # its tiles need fewer splits than the first's
+    out, ref = _random_prefill(cuda_device, B=2, H=3, D=D, bs=16, T=200, dtype=torch.bfloat16,
+                               prefixes=[1500, 20], curs=[200, 130], seed=5 + D)
+    _check(out, ref, torch.bfloat16)
+    assert b2pa.read_status(cuda_device) == 0
