@@ -123,6 +123,52 @@ def _attention_case(ref, *, seed, B, H, D, bs, initial_blocks, prefix, T, cur, d
     }
 
 
+def _model_case(ref_path: str, *, tiny: bool) -> dict:
+    """Greedy cached generation by the reference itself on CPU with its torch
+    paged attention (backend "paged_reference"): BASELINE config[0], or the
+    reference's own test model (tests/test_paged_attention.py:10-38)."""
+    import hashlib
+
+    from src.inference.generate_with_cache import generate_with_cache
+    from src.model.transformer import TinyTransformerLM
+    from src.utils.seed import set_seed
+
+    set_seed(42)
+    if tiny:
+        model = TinyTransformerLM(128, 64, 4, 2, 128, 128, attention_backend="paged_reference", kv_block_size=8,
+                                  kv_pool_initial_blocks=8, kv_pool_growth_factor=2.0)
+        prompt = torch.randint(0, 128, (2, 16))
+        new_tokens = 6
+    else:
+        model = TinyTransformerLM(5000, 512, 8, 6, 2048, 1024, attention_backend="paged_reference",
+                                  kv_block_size=16, kv_pool_initial_blocks=64, kv_pool_growth_factor=2.0)
+        prompt = torch.randint(0, 5000, (1, 128))
+        new_tokens = 128
+    model.eval()
+    h = hashlib.sha256()
+    for name, t in model.state_dict().items():
+        h.update(name.encode())
+        h.update(t.detach().contiguous().numpy().tobytes())
+    seen = []
+    hook = model.lm_head.register_forward_hook(lambda m, i, o: seen.append(o.detach()[:, -1, :].clone()))
+    res = generate_with_cache(model, prompt, max_new_tokens=new_tokens)
+    hook.remove()
+    gen = torch.stack([ids[prompt.shape[1]:] for ids in res["generated_ids"]])
+    last = torch.stack(seen)                       # [steps, B, vocab] logits at the last position
+    top2 = torch.topk(last, 2, dim=-1).values
+    margins = (top2[..., 0] - top2[..., 1]).numpy()
+    # the KV pool of layer 0 after generation, as a digest (the pools are large)
+    caches = res["kv_caches"]
+    k0 = caches[0].pool.k_blocks.contiguous().numpy()
+    return {
+        "weights_sha256": np.frombuffer(h.hexdigest().encode(), dtype=np.uint8),
+        "prompt": prompt.numpy(), "tokens": gen.numpy(),
+        "prefill_logits": last[0].numpy(), "final_logits": last[-1].numpy(),
+        "margins": margins, "layer0_k_pool_sum": np.float64(k0.astype(np.float64).sum()),
+        "layer0_block_ids": np.array(caches[0].states[0].block_ids, dtype=np.int32),
+    }
+
+
 CASES = {
     "alloc_sequence": case_alloc_sequence,
     "decode_f32_bs8_d16": lambda ref: _attention_case(ref, seed=2, B=4, H=2, D=16, bs=8, initial_blocks=4,
@@ -141,7 +187,10 @@ CASES = {
     "decode_bf16_bs16_d128": lambda ref: _attention_case(ref, seed=8, B=3, H=2, D=128, bs=16, initial_blocks=8,
                                                          prefix=[1, 31, 64], T=1, cur=[1, 1, 1],
                                                          dtype=torch.bfloat16),
+    "model_tiny": lambda ref: _model_case(REF_PATH[0], tiny=True),
+    "model_config0": lambda ref: _model_case(REF_PATH[0], tiny=False),
 }
+REF_PATH = ["/root/reference"]
 
 
 def main() -> int:
@@ -150,6 +199,7 @@ def main() -> int:
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
     torch.set_num_threads(1)
+    REF_PATH[0] = args.reference
     ref = _import_reference(args.reference)
     for name, fn in CASES.items():
         if args.only and name != args.only:
