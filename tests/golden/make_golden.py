@@ -169,6 +169,43 @@ def _model_case(ref_path: str, *, tiny: bool) -> dict:
     }
 
 
+def _serving_case() -> dict:
+    """BASELINE config[3] request stream from the reference's load generator,
+    and the reference's ContinuousBatchingScheduler(8, 256, 1536) run with the
+    deterministic fake executors of oracle/serving.py (no model): pins the
+    load generator and the scheduling policy."""
+    sys.path.insert(0, str(OUT_DIR.parent.parent))
+    from oracle import serving as osv
+    from src.config import RequestWorkloadProfile
+    from src.serving.loadgen import generate_requests
+    from src.serving.metrics import percentile
+    from src.serving.scheduler import ContinuousBatchingScheduler
+
+    profiles = [RequestWorkloadProfile(p.name, p.prompt_len_min, p.prompt_len_max, p.max_new_tokens_min,
+                                       p.max_new_tokens_max, p.weight) for p in osv.CONFIG3_PROFILES]
+    reqs = generate_requests(200, 52.0, 5000, workload_profiles=profiles, seed=42)
+    rec = {
+        "arrival_ms": np.array([r.arrival_time_ms for r in reqs]),
+        "prompt_len": np.array([r.prompt_len for r in reqs], dtype=np.int64),
+        "max_new_tokens": np.array([r.max_new_tokens for r in reqs], dtype=np.int64),
+        "prompt_id_sums": np.array([int(r.prompt_ids.sum()) for r in reqs], dtype=np.int64),
+        "first_prompt": reqs[0].prompt_ids.numpy(),
+        "workload": np.array([r.workload_name for r in reqs]),
+    }
+    sched = ContinuousBatchingScheduler(max_batch_size=8, prefill_chunk_size=256, max_tokens_per_iteration=1536)
+    done, events = sched.run(reqs, prefill_executor=osv.fake_prefill_executor,
+                             decode_executor=osv.fake_decode_executor)
+    rec["ev_phase"] = np.array([e["phase"] for e in events])
+    rec["ev_batch_size"] = np.array([e["batch_size"] for e in events], dtype=np.int64)
+    rec["ev_dispatch_ms"] = np.array([e["dispatch_time_ms"] for e in events])
+    rec["ev_tokens"] = np.array([e["tokens_scheduled"] for e in events], dtype=np.int64)
+    rec["first_token_ms"] = np.array([r.first_token_time_ms for r in done])
+    rec["finish_ms"] = np.array([r.finish_time_ms for r in done])
+    ttft = [r.first_token_latency_ms for r in done if r.first_token_time_ms is not None]
+    rec["ttft_p50_p99"] = np.array([percentile(ttft, 50), percentile(ttft, 99)])
+    return rec
+
+
 CASES = {
     "alloc_sequence": case_alloc_sequence,
     "decode_f32_bs8_d16": lambda ref: _attention_case(ref, seed=2, B=4, H=2, D=16, bs=8, initial_blocks=4,
@@ -189,6 +226,7 @@ CASES = {
                                                          dtype=torch.bfloat16),
     "model_tiny": lambda ref: _model_case(REF_PATH[0], tiny=True),
     "model_config0": lambda ref: _model_case(REF_PATH[0], tiny=False),
+    "serving_config3": lambda ref: _serving_case(),
 }
 REF_PATH = ["/root/reference"]
 

@@ -1,0 +1,84 @@
+"""BASELINE config[3] on the GPU: the 200-request continuous-batching trace
+(52 req/s, the config[3] mix, seed 42) through the reference's scheduling
+policy (restated in oracle/serving.py, pinned on CPU) on the config[0] model
+with the b2pa backend.  Every request completes with its token budget; one
+attention call in eight is shadowed by the torch restatement of the
+reference's attention on the same inputs (rtol 1e-4 / atol 1e-5).  Reports
+tokens/s and p50/p99 time to first token, the virtual clock advanced by
+measured GPU time as in the reference."""
+from __future__ import annotations
+
+import json
+import os
+import time
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import model as om
+from oracle import serving as osv
+from oracle import torch_paged as tp
+
+pytestmark = pytest.mark.gpu
+
+
+def test_config3_serving_trace(cuda_device):
+    base = om.b2pa_backend()
+    shadow = {"n": 0, "checked": 0, "max_err": 0.0}
+
+    def attention(q, kv, cur):
+        out = base.attention(q, kv, cur)
+        shadow["n"] += 1
+        if shadow["n"] % 8 == 1:
+            ref = tp.paged_attention_torch(q, kv, cur)
+            np.testing.assert_allclose(out.cpu().numpy(), ref.cpu().numpy(), rtol=1e-4, atol=1e-5)
+            shadow["checked"] += 1
+            shadow["max_err"] = max(shadow["max_err"], float((out - ref).abs().max()))
+        return out
+
+    backend = om.Backend("b200_paged", base.pool_cls, base.state_cls, base.batch_cls, attention)
+    model, _ = om.config0_model(backend, cuda_device)
+    ex = osv.ModelExecutors(model, cuda_device)
+    # warm-up as the reference's harness does (experiments/batching/benchmark_scheduler.py:43-61)
+    warm = osv.generate_requests(8, 1000.0, 5000, [osv.WorkloadProfile("w", 256, 256, 2, 2, 1.0)], seed=1)
+    osv.ContinuousScheduler(8, 256, 1536).run(warm, ex.prefill, ex.decode, ex.release)
+    # pass 1: parity -- shadow-check one attention call in eight
+    model.pools = None
+    reqs = osv.generate_requests(200, 52.0, 5000, osv.CONFIG3_PROFILES, seed=42)
+    done, _ = osv.ContinuousScheduler(8, 256, 1536).run(reqs, ex.prefill, ex.decode, ex.release)
+    assert len(done) == 200
+    assert all(r.num_generated_tokens == r.max_new_tokens for r in done)
+    assert shadow["checked"] > 100
+    # pass 2: timing -- the b2pa attention alone inside the timed model calls
+    model_t, _ = om.config0_model(base, cuda_device)
+    ex = osv.ModelExecutors(model_t, cuda_device)
+    osv.ContinuousScheduler(8, 256, 1536).run(
+        osv.generate_requests(8, 1000.0, 5000, [osv.WorkloadProfile("w", 256, 256, 2, 2, 1.0)], seed=1),
+        ex.prefill, ex.decode, ex.release)
+    model_t.pools = None
+    reqs = osv.generate_requests(200, 52.0, 5000, osv.CONFIG3_PROFILES, seed=42)
+    t0 = time.perf_counter()
+    done, events = osv.ContinuousScheduler(8, 256, 1536).run(reqs, ex.prefill, ex.decode, ex.release)
+    wall = time.perf_counter() - t0
+    assert len(done) == 200
+    assert all(r.num_generated_tokens == r.max_new_tokens for r in done)
+    assert all(r.first_token_time_ms is not None for r in done)
+    import b2pa
+
+    assert b2pa.read_status(cuda_device) == 0
+    ttft = [r.first_token_latency_ms for r in done]
+    report = {
+        "config": "BASELINE config[3]: 200 requests @52 req/s, config[3] mix, ContinuousBatchingScheduler(8, 256, 1536), "
+                  "config[0] model FP32, b2pa backend, one B200",
+        "throughput_tokens_per_s": osv.throughput_tokens_per_s(done),
+        "ttft_p50_ms": osv.percentile(ttft, 50), "ttft_p99_ms": osv.percentile(ttft, 99),
+        "latency_p99_ms": osv.percentile([r.latency_ms for r in done], 99),
+        "events": len(events), "decode_events": sum(1 for e in events if e[0] == "decode"),
+        "virtual_gpu_ms": sum(e[3] for e in events), "wall_s": wall,
+        "shadow_checked_attention_calls": shadow["checked"], "shadow_max_abs_err": shadow["max_err"],
+    }
+    print(json.dumps(report))
+    if os.path.isdir("gpurun_out"):
+        with open("gpurun_out/serving_config3.json", "w") as f:
+            json.dump(report, f)
