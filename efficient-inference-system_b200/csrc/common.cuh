@@ -176,6 +176,14 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
       : "memory");
 }
 
+// 2^x with the hardware approximation (PTX ex2.approx.ftz.f32: relative
+// error about 2^-22, subnormal results flushed to zero), for softmax weights.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // ------------------------------------------------------------ warp utils ---
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll

@@ -55,6 +55,7 @@ struct PfTcParams {
   // prefill_combine_kernel merges.
   int kt_per_split;
   int nsplit_max;
+  int max_cta_pages;  // capacity of the block-id array staged in shared memory
   float* part_o;   // [B, H, T, nsplit_max, D]
   float* part_ml;  // [B, H, T, nsplit_max, 2]
 };
@@ -82,19 +83,25 @@ struct PfTcCfg {
   static constexpr int BN = 64;          // keys per tile
   static constexpr int KB = D / 64;      // 128-byte column blocks of a row
   static constexpr int PAGES = BN / BS;  // pages per key tile
-  static constexpr int STAGES = 2;
+  static constexpr int STAGES = 3;       // K/V ring
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int P_BYTES = BM * BN * 2;
+  static constexpr int P_BYTES = BM * BN * 2;  // one P buffer; two are kept
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
   static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_P + P_BYTES;
-  static constexpr int N_BARS = 2 * STAGES + 3;
+  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
+  // kv_full[STAGES], kv_empty[STAGES], s_full[2], p_full[2], o_full[2]
+  static constexpr int N_BARS = 2 * STAGES + 6;
   static constexpr int OFF_MISC = OFF_BAR + 8 * N_BARS;
-  static constexpr int SMEM = OFF_MISC + 16 + 1024;  // + alignment slack
-  static constexpr int TMEM_COLS = (BN + D) <= 128 ? 128 : 256;
+  static constexpr int OFF_BLK = OFF_MISC + 16;      // int32 block ids of the CTA's pages
+  static constexpr int SMEM_FIXED = OFF_BLK + 1024;  // + alignment slack; + 4 * max_cta_pages
+  // TMEM: S[2] (BN columns each) then the O accumulator (D columns).
+  static constexpr int TMEM_USED = 2 * BN + D;
+  static constexpr int TMEM_COLS = TMEM_USED <= 256 ? 256 : 512;
+  // Two CTAs per SM where shared memory allows it (head_dim 64).
+  static constexpr int MIN_BLOCKS = D == 64 ? 2 : 1;
   static constexpr int THREADS = 192;
   static_assert(D == 64 || D == 128, "tcgen05 prefill is built for head_dim 64 and 128");
   static_assert(BN % BS == 0, "block size must divide the key tile");
@@ -109,7 +116,7 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int32_
 }
 
 template <typename T, int D, int BS>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192, PfTcCfg<D, BS>::MIN_BLOCKS)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             PfTcParams p) {
   using C = PfTcCfg<D, BS>;
@@ -123,11 +130,13 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
   uint64_t* kv_full = bars;
   uint64_t* kv_empty = bars + C::STAGES;
-  uint64_t* s_full = bars + 2 * C::STAGES;
-  uint64_t* p_full = s_full + 1;
-  uint64_t* o_full = s_full + 2;
+  uint64_t* s_full = bars + 2 * C::STAGES;  // [2]
+  uint64_t* p_full = s_full + 2;            // [2]
+  uint64_t* o_full = s_full + 4;            // one phase per P.V MMA
+  uint64_t* o_final = s_full + 5;           // one phase: every P.V of the CTA done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  int* sblk = reinterpret_cast<int*>(smem + C::OFF_BLK);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.x % p.nsplit_max;
@@ -152,9 +161,11 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    mbar_init(s_full, 1);
-    mbar_init(p_full, 4);
-    mbar_init(o_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_full[i], 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -165,6 +176,24 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 4 && lane == 0) {
     tc::prefetch_tmap(&tm_k);
     tc::prefetch_tmap(&tm_v);
+  }
+  {
+    // Block ids of this CTA's pages, validated once: -1 for pages past the
+    // visible range or with an id outside the pool (reported).
+    const int64_t pg0 = (int64_t)j0 * C::PAGES;
+    const int npg = ntiles * C::PAGES;
+    for (int i = tid; i < npg; i += C::THREADS) {
+      const int64_t page = pg0 + i;
+      int blk = -1;
+      if (page * BS < kend) {
+        blk = p.page_table[(int64_t)b * p.pt_stride + page];
+        if (blk >= p.num_blocks) {
+          set_status(p.status, B2PA_ERR_BAD_BLOCK_ID);
+          blk = -1;
+        }
+      }
+      sblk[i] = blk;
+    }
   }
   if (warp < 4) {
     // Q rows -> 128B-swizzled K-major tile, zeros past T.
@@ -183,8 +212,9 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc::fence_after_sync();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem;           // columns [0, 64): S
-  const uint32_t tO = tmem + C::BN;   // columns [64, 64 + D): O tile
+  // S(j) in columns [ (j%2)*BN, +BN ); O accumulates in [ 2*BN, 2*BN + D ).
+  const uint32_t tS0 = tmem;
+  const uint32_t tO = tmem + 2 * C::BN;
 
   if (warp == 4) {
     // ------------------------------------------------------------ producer
@@ -196,15 +226,7 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t bytes = 0;
 #pragma unroll
       for (int pg = 0; pg < C::PAGES; ++pg) {
-        const int64_t page = (int64_t)(j0 + j) * C::PAGES + pg;
-        int blk = -1;
-        if (page * BS < kend) {
-          blk = p.page_table[(int64_t)b * p.pt_stride + page];
-          if (blk >= p.num_blocks) {
-            if (lane == 0) set_status(p.status, B2PA_ERR_BAD_BLOCK_ID);
-            blk = -1;
-          }
-        }
+        const int blk = sblk[j * C::PAGES + pg];
         blks[pg] = blk;
         if (blk >= 0) {
           bytes += 2u * BS * D * 2;
@@ -241,16 +263,19 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else if (warp == 5) {
     // ------------------------------------------------------------ MMA issue
+    // Order: QK(0), QK(1), then per tile j: PV(j) once P(j) is ready, then
+    // QK(j+2) into the S buffer tile j just released.  The softmax of tile
+    // j+1 therefore overlaps PV(j) and the load of tile j+2.
     constexpr int FMT = sizeof(T) == 2 && ElemTraits<T>::kDtype == B2PA_DTYPE_BF16 ? 1 : 0;
     constexpr uint32_t idesc_s = tc::idesc_f16(128, C::BN, FMT, 0, 0);
     constexpr uint32_t idesc_o = tc::idesc_f16(128, D, FMT, 0, 1);
     const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
-    for (int j = 0; j < ntiles; ++j) {
+    auto issue_qk = [&](int j) -> bool {
       const int st = j % C::STAGES;
-      const uint32_t ph = (uint32_t)(j / C::STAGES) & 1u;
-      if (!warp_wait(&kv_full[st], ph, p.status, abort_flag)) break;
+      if (!warp_wait(&kv_full[st], (uint32_t)(j / C::STAGES) & 1u, p.status, abort_flag)) return false;
       tc::fence_after_sync();
       if (lane == 0) {
+        const uint32_t tS = tS0 + (uint32_t)(j & 1) * C::BN;
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const int kb = k >> 2, kk = k & 3;
@@ -258,23 +283,37 @@ __global__ void __launch_bounds__(192, 1)
           const uint64_t bd = tc::smem_desc(aK + st * C::KV_BYTES + kb * (C::BN * 128) + kk * 32, 16, 1024);
           tc::mma_f16_ss(tS, a, bd, idesc_s, k > 0);
         }
-        tc::commit(s_full);
+        tc::commit(&s_full[j & 1]);
       }
       __syncwarp();
-      if (!warp_wait(p_full, (uint32_t)j & 1u, p.status, abort_flag)) break;
+      return true;
+    };
+    bool ok = true;
+    if (ntiles > 0) ok = issue_qk(0);
+    if (ok && ntiles > 1) ok = issue_qk(1);
+    for (int j = 0; j < ntiles && ok; ++j) {
+      const int st = j % C::STAGES;
+      if (!warp_wait(&p_full[j & 1], (uint32_t)(j >> 1) & 1u, p.status, abort_flag)) break;
       tc::fence_after_sync();
       if (lane == 0) {
+        const uint32_t aPj = aP + (uint32_t)(j & 1) * C::P_BYTES;
 #pragma unroll
         for (int k = 0; k < C::BN / 16; ++k) {
-          const uint64_t a = tc::smem_desc(aP + k * 32, 16, 1024);
+          const uint64_t a = tc::smem_desc(aPj + k * 32, 16, 1024);
           const uint64_t bd = tc::smem_desc(aV + st * C::KV_BYTES + k * 2048, C::BN * 128, 1024);
-          tc::mma_f16_ss(tO, a, bd, idesc_o, k > 0);
+          tc::mma_f16_ss(tO, a, bd, idesc_o, j > 0 || k > 0);
         }
         tc::commit(o_full);
         tc::commit(&kv_empty[st]);
       }
       __syncwarp();
+      if (j + 2 < ntiles) ok = issue_qk(j + 2);
     }
+    // The epilogue cannot wait on o_full by parity: when it runs, only
+    // P.V(ntiles-3) is known complete, so o_full may still be two phases
+    // behind.  A separate single-phase barrier marks "all MMAs done".
+    if (ok && ntiles > 0 && lane == 0) tc::commit(o_final);
+    __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax
     const int r = tid;
@@ -282,15 +321,26 @@ __global__ void __launch_bounds__(192, 1)
     int64_t row_end = L < past + t + 1 ? L : past + t + 1;
     if (row_end > cap) row_end = cap;
     const uint32_t trow = (uint32_t)(warp * 32) << 16;
-    float o[D];
-#pragma unroll
-    for (int i = 0; i < D; ++i) o[i] = 0.f;
+    // O accumulates in TMEM at the scale 2^m_ref.  m_ref only moves when a
+    // tile's row max exceeds it by more than kRescale (log2 units), so the
+    // P values stay below 2^kRescale and the rescale of O (TMEM load, scale,
+    // store) is rare.  Rescaling at tile j waits for P.V(j-1): the o_full
+    // barrier completes one phase per P.V; S(j) being ready implies every MMA
+    // issued before QK(j) -- so P.V(j-2) -- is done, and P.V(j) cannot start
+    // before this warp releases P(j), so o_full is in phase j-1 or j and the
+    // parity wait is exact.
+    constexpr float kRescale = 8.f;
     float m = -INFINITY, l = 0.f;
+    bool ok = true;
     for (int j = 0; j < ntiles; ++j) {
-      if (!warp_wait(s_full, (uint32_t)j & 1u, p.status, abort_flag)) break;
+      if (!warp_wait(&s_full[j & 1], (uint32_t)(j >> 1) & 1u, p.status, abort_flag)) {
+        ok = false;
+        break;
+      }
       tc::fence_after_sync();
       float s[64];
       {
+        const uint32_t tS = tS0 + (uint32_t)(j & 1) * C::BN;
         float a[32], c[32];
         tc::tmem_ld32(tS + trow, a);
         tc::tmem_ld32(tS + trow + 32, c);
@@ -302,58 +352,92 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       const int64_t k0 = (int64_t)(j0 + j) * C::BN;
+      bool all_pages = true;
       bool page_ok[C::PAGES];
 #pragma unroll
       for (int pg = 0; pg < C::PAGES; ++pg) {
-        const int64_t page = k0 / BS + pg;
-        bool ok = false;
-        if (page * BS < kend) {
-          const int blk = p.page_table[(int64_t)b * p.pt_stride + page];
-          ok = blk >= 0 && blk < p.num_blocks;
-        }
-        page_ok[pg] = ok;
+        page_ok[pg] = sblk[j * C::PAGES + pg] >= 0;
+        all_pages = all_pages && page_ok[pg];
       }
+      // Keys of this tile visible to this row: [0, lim) (and pages present).
+      const int64_t lim64 = row_end - k0;
+      const int lim = lim64 < 0 ? 0 : (lim64 > C::BN ? C::BN : (int)lim64);
       float mt = -INFINITY;
+      if (lim == C::BN && all_pages) {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const bool vis = (k0 + i < row_end) && page_ok[i / BS];
-        s[i] = vis ? s[i] * p.scale_log2 : -INFINITY;
-        mt = fmaxf(mt, s[i]);
+        for (int i = 0; i < 64; ++i) {
+          s[i] *= p.scale_log2;
+          mt = fmaxf(mt, s[i]);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          const bool vis = i < lim && page_ok[i / BS];
+          s[i] = vis ? s[i] * p.scale_log2 : -INFINITY;
+          mt = fmaxf(mt, s[i]);
+        }
       }
-      const float m_new = fmaxf(m, mt);
-      const bool live = m_new != -INFINITY;
-      const float alpha = live ? exp2f(m - m_new) : 1.f;
+      // A row moves its reference max when the tile's max exceeds it by more
+      // than kRescale.  Rows that already hold O at the old scale need O and
+      // l multiplied by 2^(m_old - m_new); a row with no visible key so far
+      // (m = -inf) holds zeros and just adopts the new max.  TMEM accesses
+      // and the barrier wait are warp-collective, so the whole warp takes
+      // the branch if any lane needs it (other lanes scale by 1).
+      const bool need = mt > m + kRescale;
+      const float m_new = need ? mt : m;
+      const bool scale_o = need && m != -INFINITY;
+      if (j > 0 && __any_sync(kFullMask, scale_o)) {
+        const float alpha = scale_o ? fast_exp2(m - m_new) : 1.f;
+        // wait for P.V(j-1) before touching O
+        if (!warp_wait(o_full, (uint32_t)(j - 1) & 1u, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+#pragma unroll
+        for (int cb = 0; cb < D / 32; ++cb) {
+          float ov[32];
+          tc::tmem_ld32(tO + trow + cb * 32, ov);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
+          tc::tmem_st32(tO + trow + cb * 32, ov);
+        }
+        tc::tmem_wait_st();
+        l *= alpha;
+      }
+      m = m_new;
+      const bool live = m != -INFINITY;
       float lsum = 0.f;
+      unsigned char* sPj = sP + (j & 1) * C::P_BYTES;  // free: S(j) ready implies P.V(j-2) done
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) {
         float pv[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
-          pv[e] = live ? exp2f(s[c8 * 8 + e] - m_new) : 0.f;
+          pv[e] = live ? fast_exp2(s[c8 * 8 + e] - m) : 0.f;
           lsum += pv[e];
         }
         Vec<T, 8> w;
         w.from_float(pv);
-        *reinterpret_cast<uint4*>(sP + tc::sw128_offset(r, c8)) = w.w;
+        *reinterpret_cast<uint4*>(sPj + tc::sw128_offset(r, c8)) = w.w;
       }
-      l = l * alpha + lsum;
-      m = m_new;
+      l += lsum;
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
-      if (!warp_wait(o_full, (uint32_t)j & 1u, p.status, abort_flag)) break;
+      if (lane == 0) mbar_arrive(&p_full[j & 1]);
+    }
+    float o[D];
+#pragma unroll
+    for (int i = 0; i < D; ++i) o[i] = 0.f;
+    if (ok && ntiles > 0 && warp_wait(o_final, 0u, p.status, abort_flag)) {
       tc::fence_after_sync();
 #pragma unroll
-      for (int cb = 0; cb < D / 32; ++cb) {
-        float ot[32];
-        tc::tmem_ld32(tO + trow + cb * 32, ot);
-        tc::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[cb * 32 + i] = fmaf(o[cb * 32 + i], alpha, ot[i]);
-      }
-      tc::fence_before_sync();
+      for (int cb = 0; cb < D / 32; ++cb) tc::tmem_ld32(tO + trow + cb * 32, *reinterpret_cast<float(*)[32]>(o + cb * 32));
+      tc::tmem_wait_ld();
     }
+    tc::fence_before_sync();
     if (t < p.T && nsplit > 1) {
       const int64_t slot = (((int64_t)b * p.H + h) * p.T + t) * p.nsplit_max + split;
       float4* po = reinterpret_cast<float4*>(p.part_o + slot * D);
@@ -462,11 +546,17 @@ int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream) {
     p.part_ml = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + plan.off_part_ml);
     p.part_o = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + plan.off_part_o);
   }
+  const int64_t ktmax = ((int64_t)a.max_pages * BS + C::BN - 1) / C::BN;
+  const int64_t kt_cta = plan.nsplit_max > 1 ? plan.kt_per_split : ktmax;
+  p.max_cta_pages = (int)((kt_cta > 0 ? kt_cta : 1) * C::PAGES);
+  const size_t smem = C::SMEM_FIXED + 4 * (size_t)p.max_cta_pages;
+  if (smem > (size_t)device_max_smem_optin())
+    return set_error(B2PA_ERR_UNSUPPORTED, "paged_prefill: %d pages per CTA exceed shared memory", p.max_cta_pages);
   auto kern = paged_prefill_tc_kernel<T, D, BS>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill_tc smem attribute: %s", cudaGetErrorString(e));
   dim3 grid(((a.T + C::BM - 1) / C::BM) * plan.nsplit_max, a.H, a.B);
-  kern<<<grid, C::THREADS, C::SMEM, stream>>>(tmk, tmv, p);
+  kern<<<grid, C::THREADS, smem, stream>>>(tmk, tmv, p);
   if (plan.nsplit_max > 1) {
     const int64_t rows = (int64_t)a.B * a.H * a.T;
     prefill_combine_kernel<T, D, BS><<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(p);
