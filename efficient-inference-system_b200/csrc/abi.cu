@@ -64,6 +64,23 @@ int device_max_smem_optin() {
   return cache[dev];
 }
 
+int set_max_dynamic_smem_cached(const void* func, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;  // (kernel, device) -> bytes already allowed
+  const auto key = std::make_pair(func, current_device());
+  {
+    std::lock_guard<std::mutex> g(mu);
+    auto it = done.find(key);
+    if (it != done.end() && it->second >= bytes) return B2PA_OK;
+  }
+  cudaError_t e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "cudaFuncSetAttribute(%d bytes): %s", bytes, cudaGetErrorString(e));
+  std::lock_guard<std::mutex> g(mu);
+  int& v = done[key];
+  if (bytes > v) v = bytes;
+  return B2PA_OK;
+}
+
 int decode_occupancy_cached(const void* func, int threads, size_t smem) {
   static std::mutex mu;
   static std::map<std::tuple<const void*, int, size_t, int>, int> cache;
@@ -128,10 +145,10 @@ bool prefill_uses_tensor_cores(int D, int block_size, int dtype, int64_t pool_ro
 }
 
 // Split the key range of the tensor-core prefill when the (query tile, head,
-// sequence) CTAs alone would leave most of the machine idle.  The kernel runs
-// one CTA per SM, so the split CTAs must still fit in one wave of a 148-SM
-// part (extra waves cost more than the shorter key walks save); at least 2
-// key tiles per CTA.
+// sequence) CTAs alone would leave most SMs idle.  The split CTAs must fit in
+// one wave of one CTA per SM of a 148-SM part: measured on config[2], a second
+// wave or a second resident CTA per SM costs more (combine pass, shared SM)
+// than the shorter key walks save.  At least 2 key tiles per CTA.
 PrefillPlan make_prefill_plan(int B, int H, int T, int D, int max_pages, int block_size, int dtype) {
   PrefillPlan pl;
   const int64_t ktmax = ((int64_t)max_pages * block_size + 63) / 64;
@@ -141,6 +158,11 @@ PrefillPlan make_prefill_plan(int B, int H, int T, int D, int max_pages, int blo
   if (!prefill_uses_tensor_cores(D, block_size, dtype, 0) || B <= 0 || T <= 0 || ktmax <= 2) return pl;
   const int64_t ctas = (int64_t)B * H * ((T + 127) / 128);
   int64_t splits = 148 / ctas;
+  // A CTA stages the block ids of its key range in shared memory: at most
+  // 1024 key tiles (64k keys) per CTA.
+  const int64_t kt_cap = 1024;
+  const int64_t min_splits = (ktmax + kt_cap - 1) / kt_cap;
+  if (splits < min_splits) splits = min_splits;
   if (splits > ktmax) splits = ktmax;
   if (splits <= 1) return pl;
   int64_t kt = (ktmax + splits - 1) / splits;

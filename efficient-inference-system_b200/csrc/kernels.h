@@ -16,6 +16,10 @@ namespace b2pa {
 // `code` so callers can `return set_error(code, ...)`.
 int set_error(int code, const char* fmt, ...);
 
+// cudaFuncSetAttribute(MaxDynamicSharedMemorySize) once per kernel and
+// device (the call costs microseconds; launches are hot).
+int set_max_dynamic_smem_cached(const void* func, int bytes);
+
 // Multiprocessor count of the current device (cached per device).
 int device_sm_count();
 

@@ -540,8 +540,9 @@ int launch_decode_impl(const AttnArgs& a, const DecodePlan& plan, cudaStream_t s
   const int threads = (plan.G + 1) * 32;
 
   auto kern = paged_decode_kernel<T, D, BS>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_decode smem attribute: %s", cudaGetErrorString(e));
+  int rc_attr = set_max_dynamic_smem_cached(reinterpret_cast<const void*>(kern), (int)smem);
+  if (rc_attr != B2PA_OK) return rc_attr;
+  cudaError_t e;
   const int per_sm = decode_occupancy_cached(reinterpret_cast<const void*>(kern), threads, smem);
   if (per_sm <= 0) return set_error(B2PA_ERR_UNSUPPORTED, "paged_decode: kernel does not fit on an SM");
   int64_t grid = (int64_t)device_sm_count() * per_sm;

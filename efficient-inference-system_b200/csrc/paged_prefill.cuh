@@ -226,8 +226,9 @@ int launch_prefill_simt(const AttnArgs& a, cudaStream_t stream) {
   if (smem > (size_t)device_max_smem_optin())
     return set_error(B2PA_ERR_UNSUPPORTED, "paged_prefill: %zu bytes of shared memory exceed the device limit", smem);
   auto kern = paged_prefill_simt_kernel<T, D, BS>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill smem attribute: %s", cudaGetErrorString(e));
+  int rc_attr = set_max_dynamic_smem_cached(reinterpret_cast<const void*>(kern), (int)smem);
+  if (rc_attr != B2PA_OK) return rc_attr;
+  cudaError_t e;
   dim3 grid((a.T + kPfTQ - 1) / kPfTQ, a.H, a.B);
   kern<<<grid, kPfThreads, smem, stream>>>(p);
   e = cudaGetLastError();

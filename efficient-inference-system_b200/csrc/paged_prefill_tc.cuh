@@ -83,7 +83,9 @@ struct PfTcCfg {
   static constexpr int BN = 64;          // keys per tile
   static constexpr int KB = D / 64;      // 128-byte column blocks of a row
   static constexpr int PAGES = BN / BS;  // pages per key tile
-  static constexpr int STAGES = 3;       // K/V ring
+  // K/V ring depth: a stage is refilled only after the P.V MMA that read it,
+  // so the load of tile j+STAGES overlaps the softmax of STAGES tiles.
+  static constexpr int STAGES = D == 64 ? 6 : 4;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
   static constexpr int P_BYTES = BM * BN * 2;  // one P buffer; two are kept
@@ -100,8 +102,7 @@ struct PfTcCfg {
   // TMEM: S[2] (BN columns each) then the O accumulator (D columns).
   static constexpr int TMEM_USED = 2 * BN + D;
   static constexpr int TMEM_COLS = TMEM_USED <= 256 ? 256 : 512;
-  // Two CTAs per SM where shared memory allows it (head_dim 64).
-  static constexpr int MIN_BLOCKS = D == 64 ? 2 : 1;
+  static constexpr int MIN_BLOCKS = 1;
   static constexpr int THREADS = 192;
   static_assert(D == 64 || D == 128, "tcgen05 prefill is built for head_dim 64 and 128");
   static_assert(BN % BS == 0, "block size must divide the key tile");
@@ -362,21 +363,24 @@ __global__ void __launch_bounds__(192, PfTcCfg<D, BS>::MIN_BLOCKS)
       // Keys of this tile visible to this row: [0, lim) (and pages present).
       const int64_t lim64 = row_end - k0;
       const int lim = lim64 < 0 ? 0 : (lim64 > C::BN ? C::BN : (int)lim64);
-      float mt = -INFINITY;
       if (lim == C::BN && all_pages) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          s[i] *= p.scale_log2;
-          mt = fmaxf(mt, s[i]);
-        }
+        for (int i = 0; i < 64; ++i) s[i] *= p.scale_log2;
       } else {
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
           const bool vis = i < lim && page_ok[i / BS];
           s[i] = vis ? s[i] * p.scale_log2 : -INFINITY;
-          mt = fmaxf(mt, s[i]);
         }
       }
+      // Row max as a tree (short dependency chains: one warp per SM
+      // sub-partition runs this, so latency, not throughput, bounds it).
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = fmaxf(fmaxf(s[i], s[i + 8]), fmaxf(s[i + 16], s[i + 24]));
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], fmaxf(fmaxf(s[i + 32], s[i + 40]), fmaxf(s[i + 48], s[i + 56])));
+      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       // A row moves its reference max when the tile's max exceeds it by more
       // than kRescale.  Rows that already hold O at the old scale need O and
       // l multiplied by 2^(m_old - m_new); a row with no visible key so far
@@ -408,7 +412,9 @@ __global__ void __launch_bounds__(192, PfTcCfg<D, BS>::MIN_BLOCKS)
       }
       m = m_new;
       const bool live = m != -INFINITY;
-      float lsum = 0.f;
+      float ls[8];  // 8 independent partial sums
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ls[e] = 0.f;
       unsigned char* sPj = sP + (j & 1) * C::P_BYTES;  // free: S(j) ready implies P.V(j-2) done
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) {
@@ -416,13 +422,13 @@ __global__ void __launch_bounds__(192, PfTcCfg<D, BS>::MIN_BLOCKS)
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
           pv[e] = live ? fast_exp2(s[c8 * 8 + e] - m) : 0.f;
-          lsum += pv[e];
+          ls[e] += pv[e];
         }
         Vec<T, 8> w;
         w.from_float(pv);
         *reinterpret_cast<uint4*>(sPj + tc::sw128_offset(r, c8)) = w.w;
       }
-      l += lsum;
+      l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
       __syncwarp();
@@ -553,8 +559,9 @@ int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream) {
   if (smem > (size_t)device_max_smem_optin())
     return set_error(B2PA_ERR_UNSUPPORTED, "paged_prefill: %d pages per CTA exceed shared memory", p.max_cta_pages);
   auto kern = paged_prefill_tc_kernel<T, D, BS>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill_tc smem attribute: %s", cudaGetErrorString(e));
+  int rc_attr = set_max_dynamic_smem_cached(reinterpret_cast<const void*>(kern), (int)smem);
+  if (rc_attr != B2PA_OK) return rc_attr;
+  cudaError_t e;
   dim3 grid(((a.T + C::BM - 1) / C::BM) * plan.nsplit_max, a.H, a.B);
   kern<<<grid, C::THREADS, smem, stream>>>(tmk, tmv, p);
   if (plan.nsplit_max > 1) {

@@ -35,7 +35,48 @@ EncodeTiledFn encode_fn() {
 
 }  // namespace
 
+namespace {
+// Recently encoded maps: a pool keeps its address until it grows, so the
+// maps of the last few pools are reused instead of re-encoded every call.
+struct MapKey {
+  const void* pool;
+  int64_t rows;
+  int D, block_size, dtype;
+  bool operator==(const MapKey& o) const {
+    return pool == o.pool && rows == o.rows && D == o.D && block_size == o.block_size && dtype == o.dtype;
+  }
+};
+constexpr int kMapCache = 16;
+std::mutex g_map_mu;
+MapKey g_keys[kMapCache];
+CUtensorMap g_maps[kMapCache];
+int g_next = 0, g_used = 0;
+}  // namespace
+
+bool encode_pool_tensor_map_uncached(CUtensorMap* map, const void* pool, int64_t rows, int D, int block_size,
+                                     int dtype);
+
 bool encode_pool_tensor_map(CUtensorMap* map, const void* pool, int64_t rows, int D, int block_size, int dtype) {
+  const MapKey key{pool, rows, D, block_size, dtype};
+  {
+    std::lock_guard<std::mutex> g(g_map_mu);
+    for (int i = 0; i < g_used; ++i)
+      if (g_keys[i] == key) {
+        *map = g_maps[i];
+        return true;
+      }
+  }
+  if (!encode_pool_tensor_map_uncached(map, pool, rows, D, block_size, dtype)) return false;
+  std::lock_guard<std::mutex> g(g_map_mu);
+  g_keys[g_next] = key;
+  g_maps[g_next] = *map;
+  g_next = (g_next + 1) % kMapCache;
+  if (g_used < kMapCache) ++g_used;
+  return true;
+}
+
+bool encode_pool_tensor_map_uncached(CUtensorMap* map, const void* pool, int64_t rows, int D, int block_size,
+                                     int dtype) {
   EncodeTiledFn fn = encode_fn();
   if (!fn || rows <= 0 || rows > ((int64_t)1 << 31)) return false;
   const CUtensorMapDataType dt = dtype == B2PA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;

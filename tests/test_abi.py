@@ -92,7 +92,7 @@ def test_workspace_size_is_monotone(lib):
     assert c > 0 and c % 256 == 0
     assert f(0, 8, 64, 65, 16, 0) == 0
     assert lib.b2pa_paged_prefill_workspace_size(8, 8, 256, 64, 64, 16, 0) == 0  # fp32: CUDA-core path, no split
-    assert lib.b2pa_paged_prefill_workspace_size(8, 8, 256, 64, 65, 16, 1) == 0  # bf16 config[2]: one full wave, no split
+    assert lib.b2pa_paged_prefill_workspace_size(8, 8, 256, 64, 65, 16, 1) == 0  # bf16 config[2]: one wave, no split
     assert lib.b2pa_paged_prefill_workspace_size(1, 8, 256, 64, 65, 16, 1) > 0   # one sequence: key-range split
 
 
