@@ -601,11 +601,37 @@ def main_secondary(args) -> int:
             line.update({"tokens_per_s": B / (step_ms / 1e3), "attention_hbm_gbs": bytes_ / (attn_ms / 1e3) / 1e9,
                          "bytes_per_launch": bytes_,
                          "frac_of_hbm_peak": bytes_ / (attn_ms / 1e3) / 1e9 / peaks["hbm_gbs"]})
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = _secondary_cpu_baseline(kp, vp, q, table, pages, lens, T, args.cpu_seconds)
         lines.append(line)
         print(json.dumps(line))
         del kp, vp, flush
         torch.cuda.empty_cache()
     return 0
+
+
+def _secondary_cpu_baseline(kp, vp, q, table, pages, lens, T, target_seconds: float) -> dict:
+    """The CPU restatement of the reference's torch path (oracle/paged_oracle.c,
+    all host threads) on the same inputs, repeated to about target_seconds."""
+    from oracle import oracle as orc
+
+    k_h = kp.float().cpu().numpy()
+    v_h = vp.float().cpu().numpy()
+    q_h = q.float().cpu().numpy()
+    tables = [[int(x) for x in table[b, :pages[b]]] for b in range(len(lens))]
+    cur = [T] * len(lens)
+    threads = orc.c_max_threads()
+    t0 = time.perf_counter()
+    orc.paged_attention_c(q_h, k_h, v_h, tables, lens.tolist(), cur, nthreads=threads)
+    one = time.perf_counter() - t0
+    reps = max(1, int(target_seconds / max(one, 1e-3)))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        orc.paged_attention_c(q_h, k_h, v_h, tables, lens.tolist(), cur, nthreads=threads)
+    sec = (time.perf_counter() - t0) / reps
+    return {"value": len(lens) * T / sec, "unit": "tok/s", "seconds_per_step": sec, "cores": threads,
+            "kind": "port", "sample": f"full step, {reps} repetitions; attention only (oracle/paged_oracle.c)",
+            "cpu_model": _cpu_model()}
 
 
 def _peaks() -> dict:
