@@ -32,13 +32,14 @@ _MAX_ENTRIES = 64
 
 
 class _Entry:
-    __slots__ = ("states", "lists", "counts", "table", "dev_table", "width")
+    __slots__ = ("states", "states_ref", "lists", "counts", "table", "dev_table", "width")
 
     def __init__(self, states, width: int):
         B = len(states)
         self.states = list(states)
+        self.states_ref = states
         self.lists = [None] * B
-        self.counts = np.zeros(B, dtype=np.int64)
+        self.counts = [0] * B
         self.width = width
         self.table = np.full((B, width), -1, dtype=np.int32)
         self.dev_table: torch.Tensor | None = None
@@ -47,26 +48,56 @@ class _Entry:
 _entries: "OrderedDict[tuple, _Entry]" = OrderedDict()
 
 
-def _refresh_rows(ent: _Entry) -> bool:
-    """Brings the host table up to date; returns True if any row changed."""
+def _refresh_rows(ent: _Entry, seq_out: np.ndarray | None = None, states=None) -> tuple[bool, int]:
+    """Brings the host table up to date in one pass over the states; returns
+    (any row changed, max block count) and fills ``seq_out`` with seq_len.
+    A max block count of -1 asks the caller to rebuild the entry (a row
+    outgrew the table, or ``states`` no longer holds the entry's states)."""
     changed = False
     table = ent.table
-    for r, s in enumerate(ent.states):
+    counts = ent.counts
+    lists = ent.lists
+    mine = ent.states
+    if states is not None and len(states) != len(mine):
+        return True, -1
+    max_pages = 0
+    for r, s in enumerate(mine if states is None else states):
+        if s is not mine[r]:
+            return True, -1
         ids = s.block_ids
         n = len(ids)
-        old = int(ent.counts[r])
-        if ids is ent.lists[r] and n == old:
+        if n > max_pages:
+            max_pages = n
+        if seq_out is not None:
+            seq_out[r] = s.seq_len
+        old = counts[r]
+        if n == old and ids is lists[r]:
             continue
-        if ids is ent.lists[r] and n > old:
+        if n > ent.width:
+            return True, -1  # caller rebuilds a wider table
+        if ids is lists[r] and n > old:
             table[r, old:n] = ids[old:n]
         else:
             table[r, :n] = ids
             if n < old:
                 table[r, n:old] = -1
-        ent.lists[r] = ids
-        ent.counts[r] = n
+        lists[r] = ids
+        counts[r] = n
         changed = True
-    return changed
+    return changed, max_pages
+
+
+def _lookup(cache, device: torch.device, stream: int) -> _Entry | None:
+    """The entry remembered on the batch object (the common case: the same
+    batch object for append and attention), else the LRU by state identity."""
+    ent = getattr(cache, "_b2pa_meta", None)
+    if ent is not None and ent[0] == (device.index, stream) and ent[1].states_ref is cache.states:
+        return ent[1]
+    key = (device.index, stream, tuple(id(s) for s in cache.states))
+    hit = _entries.get(key)
+    if hit is not None:
+        _entries.move_to_end(key)
+    return hit
 
 
 def block_table_and_lengths(cache, device: torch.device, extra: list[list[int]] | None = None):
@@ -75,23 +106,28 @@ def block_table_and_lengths(cache, device: torch.device, extra: list[list[int]] 
     with ``width >= max_pages`` (pass its row stride to the kernels)."""
     states = cache.states
     B = len(states)
-    max_pages = max((len(s.block_ids) for s in states), default=0)
-    key = (device.index, torch.cuda.current_stream(device).cuda_stream, tuple(id(s) for s in states))
-    ent = _entries.get(key)
-    if ent is None or max_pages > ent.width:
+    stream = torch.cuda.current_stream(device).cuda_stream
+    rows = 1 + (len(extra) if extra else 0)
+    small = np.empty(B * rows, dtype=np.int32)
+    ent = _lookup(cache, device, stream)
+    changed, max_pages = (True, -1) if ent is None else _refresh_rows(ent, small, states)
+    if max_pages < 0:
+        max_pages = max((len(s.block_ids) for s in states), default=0)
         width = max(max_pages, 1)
         if ent is not None:
             width = max(width, ent.width * 2)
         ent = _Entry(states, width)
+        key = (device.index, stream, tuple(id(s) for s in states))
         _entries[key] = ent
         while len(_entries) > _MAX_ENTRIES:
             _entries.popitem(last=False)
-    else:
-        _entries.move_to_end(key)
-    dirty = _refresh_rows(ent) or ent.dev_table is None
-    rows = 1 + (len(extra) if extra else 0)
-    small = np.empty(B * rows, dtype=np.int32)
-    small[:B] = [s.seq_len for s in states]
+        changed, max_pages = _refresh_rows(ent, small)
+    ent.states_ref = states
+    try:
+        cache._b2pa_meta = ((device.index, stream), ent)
+    except AttributeError:  # batch objects that refuse new attributes use the LRU only
+        pass
+    dirty = changed or ent.dev_table is None
     if extra:
         for i, row in enumerate(extra):
             small[B * (i + 1): B * (i + 2)] = row

@@ -239,14 +239,28 @@ def plan_append(cache, k_new: torch.Tensor, lengths: list[int]) -> list[int]:
     """Initialises the pool and allocates blocks request by request, in batch
     order (paged_kv.py:165-171); returns each request's start position."""
     _, H, T, D = k_new.shape
+    pool = cache.pool
+    if any(n > 0 for n in lengths):
+        pool.ensure_initialized(H, D, k_new.dtype, k_new.device)
+    bs = pool.block_size
+    allocate = pool.allocate_block
     starts = []
     for b, state in enumerate(cache.states):
-        if state.pool is not cache.pool:
+        if state.pool is not pool:
             raise ValueError("b2pa: all states of a BatchedPagedKVCache must share its pool")
-        n = max(min(lengths[b], T), 0)
-        if n > 0:
-            state.pool.ensure_initialized(H, D, k_new.dtype, k_new.device)
-        starts.append(reserve_tokens(state, n))
+        start = state.seq_len
+        starts.append(start)
+        n = lengths[b]
+        n = T if n > T else (0 if n < 0 else n)
+        if n <= 0:
+            continue
+        # one block each time the write position reaches a block boundary
+        # (paged_kv.py:110-113): blocks for positions start .. start+n-1
+        need = (start + n + bs - 1) // bs - (start + bs - 1) // bs
+        ids = state.block_ids
+        for _ in range(need):
+            ids.append(allocate())
+        state.seq_len = start + n
     return starts
 
 
