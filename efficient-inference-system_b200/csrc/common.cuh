@@ -184,6 +184,25 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// Packed two-lane fp32 arithmetic of sm_100 (one instruction for two
+// values): d = a * b + c and d = a + b, each lane rounded to nearest.
+__device__ __forceinline__ uint64_t f2_bits(float2 v) {
+  return (uint64_t)__float_as_uint(v.x) | ((uint64_t)__float_as_uint(v.y) << 32);
+}
+__device__ __forceinline__ float2 f2_from_bits(uint64_t b) {
+  return make_float2(__uint_as_float((uint32_t)b), __uint_as_float((uint32_t)(b >> 32)));
+}
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return f2_from_bits(d);
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return f2_from_bits(d);
+}
+
 // ------------------------------------------------------------ warp utils ---
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll

@@ -8,19 +8,27 @@
 // sees keys 0 .. min(seq_len, seq_len - cur_len + t + 1) - 1; rows that see
 // nothing are zero; rows past cur_len see the whole sequence).
 //
-// One CTA = (128 query rows, head, sequence); 6 warps:
-//   warp 4  producer: per 64-key tile, one TMA tensor load per page and
-//           128-byte column block for K and for V (block table gather; the
-//           pool is viewed as a 2-d [blocks*H*block_size, D] tensor with a
-//           128B-swizzle map), into a 2-stage ring;
-//   warp 5  MMA issuer (one elected lane): S = Q.K^T (M=128, N=64, K=D) into
-//           TMEM, then O_tile = P.V (M=128, N=D, K=64) into TMEM; completion
-//           signalled with tcgen05.commit on mbarriers;
-//   warps 0-3 softmax: thread r owns query row r: reads its S row from TMEM,
-//           masks, online softmax in the log2 domain, writes P (bf16/fp16,
-//           128B-swizzled K-major) to shared memory for the next MMA, and
-//           accumulates O_tile from TMEM into fp32 registers with the
-//           running rescale.  The output is divided by max(l, 1e-9).
+// One CTA = (128 query rows, head, sequence); NG softmax warpgroups (two for
+// head_dim 64, one for 128) plus three warps:
+//   K and V producer warps: per 64-key tile, one TMA tensor load per page and
+//           128-byte column block (block-table gather; the pool is viewed as a
+//           2-d [blocks*H*block_size, D] tensor with a 128B-swizzle map) into
+//           a STAGES-deep K ring and a STAGES-deep V ring.  A K stage is
+//           refilled as soon as its Q.K^T is done, well before the P.V of
+//           the same tile frees its V stage.  They read block ids straight
+//           from the table, so the first loads leave before the rest of the
+//           CTA has finished setting up;
+//   MMA warp (one elected lane): S = Q.K^T (M=128, N=64, K=D) into TMEM,
+//           issued 2*NG tiles ahead, then O_g += P.V (M=128, N=D, K=64) into
+//           the TMEM accumulator of the tile's group; completion signalled
+//           with tcgen05.commit on mbarriers;
+//   softmax warpgroups: key tile j belongs to group j % NG; thread r of a
+//           group owns query row r: reads its S row from TMEM, masks, online
+//           softmax in the log2 domain, writes P (bf16/fp16, 128B-swizzled
+//           K-major) to shared memory for the P.V MMA, and rescales its O in
+//           TMEM when its running max moves by more than 2^8.  The epilogue
+//           merges the groups' (max, denominator, O) and divides by
+//           max(l, 1e-9).
 // Q is loaded by the softmax threads (arbitrary strides) into the swizzled
 // layout.  Every mbarrier wait is bounded (1 s); a wait that gives up records
 // B2PA_ERR_DEVICE_TIMEOUT, raises a CTA-wide abort flag and the roles drain
@@ -83,30 +91,53 @@ struct PfTcCfg {
   static constexpr int BN = 64;          // keys per tile
   static constexpr int KB = D / 64;      // 128-byte column blocks of a row
   static constexpr int PAGES = BN / BS;  // pages per key tile
-  // K/V ring depth: a stage is refilled only after the P.V MMA that read it,
-  // so the load of tile j+STAGES overlaps the softmax of STAGES tiles.
+  // Softmax warpgroups.  With two, key tiles alternate between them (tile j
+  // -> group j % NG) and each keeps its own running max, denominator and O
+  // accumulator; the groups are merged in the epilogue.  Two groups put two
+  // softmax warps on every SM sub-partition, so one warp's exponentials
+  // overlap the other's TMEM loads, barrier waits and P stores.
+  static constexpr int NG = D == 64 ? 2 : 1;
+  static constexpr int NSLOT = 2 * NG;  // S/P buffers: two per group
+  // Depth of the K ring and of the V ring.  A K stage is refilled once the
+  // Q.K^T that read it is done, a V stage once its P.V is done, so each ring
+  // loads up to STAGES tiles ahead of its consumer.
   static constexpr int STAGES = D == 64 ? 6 : 4;
   static constexpr int Q_BYTES = BM * D * 2;
   static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int P_BYTES = BM * BN * 2;  // one P buffer; two are kept
+  static constexpr int P_BYTES = BM * BN * 2;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
   static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
-  static constexpr int OFF_BAR = OFF_P + 2 * P_BYTES;
-  // kv_full[STAGES], kv_empty[STAGES], s_full[2], p_full[2], o_full[2]
-  static constexpr int N_BARS = 2 * STAGES + 6;
-  static constexpr int OFF_MISC = OFF_BAR + 8 * N_BARS;
-  static constexpr int OFF_BLK = OFF_MISC + 16;      // int32 block ids of the CTA's pages
+  static constexpr int OFF_BAR = OFF_P + NSLOT * P_BYTES;
+  // k_full, k_empty, v_full, v_empty [STAGES each], s_full[NSLOT], p_full[NSLOT], o_full[NG], o_final
+  static constexpr int N_BARS = 4 * STAGES + 2 * NSLOT + NG + 1;
+  static constexpr int OFF_MISC = OFF_BAR + 8 * N_BARS;  // TMEM base, abort flag
+  static constexpr int OFF_ML = OFF_MISC + 16;           // per-group (m, l) of every row, for the merge
+  static constexpr int OFF_BLK = OFF_ML + (NG > 1 ? 2 * NG * BM * 4 : 0);  // int32 block ids of the CTA's pages
   static constexpr int SMEM_FIXED = OFF_BLK + 1024;  // + alignment slack; + 4 * max_cta_pages
-  // TMEM: S[2] (BN columns each) then the O accumulator (D columns).
-  static constexpr int TMEM_USED = 2 * BN + D;
+  // TMEM: S[NSLOT] (BN columns each), then one O accumulator per group.
+  static constexpr int TMEM_USED = NSLOT * BN + NG * D;
   static constexpr int TMEM_COLS = TMEM_USED <= 256 ? 256 : 512;
-  static constexpr int MIN_BLOCKS = 1;
-  static constexpr int THREADS = 192;
+  static constexpr int SOFTMAX_THREADS = 128 * NG;
+  static constexpr int K_WARP = 4 * NG;      // K producer (also initialises the barriers)
+  static constexpr int V_WARP = 4 * NG + 1;  // V producer
+  static constexpr int MMA_WARP = 4 * NG + 2;
+  static constexpr int THREADS = SOFTMAX_THREADS + 96;
   static_assert(D == 64 || D == 128, "tcgen05 prefill is built for head_dim 64 and 128");
-  static_assert(BN % BS == 0, "block size must divide the key tile");
+  static_assert(BN % BS == 0 && 32 % PAGES == 0, "block size must divide the key tile");
+  static_assert(TMEM_USED <= 512, "TMEM holds 512 columns");
+  static_assert(SMEM_FIXED <= 200 * 1024, "shared-memory plan");
 };
+
+// Named barriers (id 0 is __syncthreads): 1 = set-up done (every thread; the
+// producer only arrives), 2 = softmax threads.
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+__device__ __forceinline__ void named_bar_arrive(int id, int n) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
 
 // Waits with every lane of the warp; false (for all lanes) if any gave up.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int32_t* status, volatile int* abort_flag) {
@@ -116,11 +147,24 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity, int32_
   return ok;
 }
 
+// Block id of local page `i` of a CTA (page pg0 + i of sequence b): -1 when
+// past the keys the CTA reads or past the table; ids outside the pool are
+// reported and read as -1.  `raw` is the table entry (loaded early).
+__device__ __forceinline__ int prefill_checked_block(const PfTcParams& p, int raw, int64_t page, int64_t kend, int bs) {
+  if (page >= p.max_pages || page * bs >= kend) return -1;
+  if (raw >= p.num_blocks) {
+    set_status(p.status, B2PA_ERR_BAD_BLOCK_ID);
+    return -1;
+  }
+  return raw;
+}
+
 template <typename T, int D, int BS>
-__global__ void __launch_bounds__(192, PfTcCfg<D, BS>::MIN_BLOCKS)
+__global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             PfTcParams p) {
   using C = PfTcCfg<D, BS>;
+  constexpr int NG = C::NG, NSLOT = C::NSLOT;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -129,14 +173,17 @@ __global__ void __launch_bounds__(192, PfTcCfg<D, BS>::MIN_BLOCKS)
   unsigned char* sV = smem + C::OFF_V;
   unsigned char* sP = smem + C::OFF_P;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* kv_full = bars;
-  uint64_t* kv_empty = bars + C::STAGES;
-  uint64_t* s_full = bars + 2 * C::STAGES;  // [2]
-  uint64_t* p_full = s_full + 2;            // [2]
-  uint64_t* o_full = s_full + 4;            // one phase per P.V MMA
-  uint64_t* o_final = s_full + 5;           // one phase: every P.V of the CTA done
+  uint64_t* k_full = bars;
+  uint64_t* k_empty = bars + C::STAGES;
+  uint64_t* v_full = bars + 2 * C::STAGES;
+  uint64_t* v_empty = bars + 3 * C::STAGES;
+  uint64_t* s_full = bars + 4 * C::STAGES;  // [NSLOT]
+  uint64_t* p_full = s_full + NSLOT;        // [NSLOT]
+  uint64_t* o_full = p_full + NSLOT;        // [NG]: one phase per P.V MMA of the group
+  uint64_t* o_final = o_full + NG;          // one phase: every P.V of the CTA done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
+  float* sML = reinterpret_cast<float*>(smem + C::OFF_ML);
   int* sblk = reinterpret_cast<int*>(smem + C::OFF_BLK);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -144,6 +191,18 @@ __global__ void __launch_bounds__(192, PfTcCfg<D, BS>::MIN_BLOCKS)
   const int t0 = (blockIdx.x / p.nsplit_max) * C::BM;
   const int h = blockIdx.y;
   const int b = blockIdx.z;
+  const int j0 = split * p.kt_per_split;
+  const int64_t pg0 = (int64_t)j0 * C::PAGES;
+  const int32_t* pt_row = p.page_table + (int64_t)b * p.pt_stride;
+
+  // Table entries of the first pages, read before the sequence length is
+  // known so that both loads are in flight together (the producer: one page
+  // per lane; the softmax threads: one page each, staged below).
+  int blk_pre = -1;
+  {
+    const int i = warp == C::K_WARP || warp == C::V_WARP ? lane : tid;
+    if (warp != C::MMA_WARP && pg0 + i < p.max_pages) blk_pre = pt_row[pg0 + i];
+  }
 
   const int64_t L = p.seq_lens[b];
   const int64_t past = L - (int64_t)p.cur_lens[b];
@@ -152,102 +211,77 @@ __global__ void __launch_bounds__(192, PfTcCfg<D, BS>::MIN_BLOCKS)
   int ntiles_all, nsplit;
   prefill_tile_range(p, b, t0, C::BM, C::BN, BS, &kend, &ntiles_all, &nsplit);
   if (split >= nsplit) return;  // this query tile needs fewer splits (uniform across the CTA)
-  const int j0 = split * p.kt_per_split;
   const int j1 = (j0 + p.kt_per_split < ntiles_all) ? j0 + p.kt_per_split : ntiles_all;
   const int ntiles = j1 > j0 ? j1 - j0 : 0;  // tiles of this CTA; tile index = j0 + local
 
-  if (tid == 0) {
-    if (L > cap) set_status(p.status, B2PA_ERR_BAD_BLOCK_ID);
-    for (int s = 0; s < C::STAGES; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
-    }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 4);
-      mbar_init(&o_full[i], 1);
-    }
-    *abort_flag = 0;
-    fence_mbar_init();
-  }
-  if (warp == 5) {
-    tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tc::tmem_relinquish();
-  }
-  if (warp == 4 && lane == 0) {
-    tc::prefetch_tmap(&tm_k);
-    tc::prefetch_tmap(&tm_v);
-  }
-  {
-    // Block ids of this CTA's pages, validated once: -1 for pages past the
-    // visible range or with an id outside the pool (reported).
-    const int64_t pg0 = (int64_t)j0 * C::PAGES;
-    const int npg = ntiles * C::PAGES;
-    for (int i = tid; i < npg; i += C::THREADS) {
-      const int64_t page = pg0 + i;
-      int blk = -1;
-      if (page * BS < kend) {
-        blk = p.page_table[(int64_t)b * p.pt_stride + page];
-        if (blk >= p.num_blocks) {
-          set_status(p.status, B2PA_ERR_BAD_BLOCK_ID);
-          blk = -1;
+  if (warp == C::K_WARP || warp == C::V_WARP) {
+    // ----------------------------------------------------------- producers
+    const bool is_k = warp == C::K_WARP;
+    if (is_k) {
+      if (lane == 0) {
+        if (L > cap) set_status(p.status, B2PA_ERR_BAD_BLOCK_ID);
+        for (int s = 0; s < C::STAGES; ++s) {
+          mbar_init(&k_full[s], 1);
+          mbar_init(&k_empty[s], 1);
+          mbar_init(&v_full[s], 1);
+          mbar_init(&v_empty[s], 1);
         }
+        for (int i = 0; i < NSLOT; ++i) {
+          mbar_init(&s_full[i], 1);
+          mbar_init(&p_full[i], 4);
+        }
+        for (int g = 0; g < NG; ++g) mbar_init(&o_full[g], 1);
+        mbar_init(o_final, 1);
+        *abort_flag = 0;
+        fence_mbar_init();
+        tc::prefetch_tmap(&tm_k);
+        tc::prefetch_tmap(&tm_v);
       }
-      sblk[i] = blk;
+      __syncwarp();
+      named_bar_arrive(1, C::THREADS);
+    } else {
+      named_bar_sync(1, C::THREADS);  // barriers initialised
     }
-  }
-  if (warp < 4) {
-    // Q rows -> 128B-swizzled K-major tile, zeros past T.
-    const int r = tid;
-    const int t = t0 + r;
-    const T* qrow = static_cast<const T*>(p.q) + (int64_t)b * p.sq_b + (int64_t)h * p.sq_h + (int64_t)t * p.sq_t;
-#pragma unroll
-    for (int c = 0; c < D / 8; ++c) {
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (t < p.T) v = *reinterpret_cast<const uint4*>(qrow + c * 8);
-      *reinterpret_cast<uint4*>(sQ + (c >> 3) * (C::BM * 128) + tc::sw128_offset(r, c & 7)) = v;
-    }
-    tc::fence_proxy_async_smem();
-  }
-  tc::fence_before_sync();
-  __syncthreads();
-  tc::fence_after_sync();
-  const uint32_t tmem = *tmem_slot;
-  // S(j) in columns [ (j%2)*BN, +BN ); O accumulates in [ 2*BN, 2*BN + D ).
-  const uint32_t tS0 = tmem;
-  const uint32_t tO = tmem + 2 * C::BN;
-
-  if (warp == 4) {
-    // ------------------------------------------------------------ producer
+    unsigned char* ring = is_k ? sK : sV;
+    const CUtensorMap* tmap = is_k ? &tm_k : &tm_v;
+    uint64_t* full = is_k ? k_full : v_full;
+    uint64_t* empty = is_k ? k_empty : v_empty;
+    // Block ids in registers, 32 pages at a time (lane i: page chunk*32+i).
+    int chunk = 0;
+    int blk_lane = prefill_checked_block(p, blk_pre, pg0 + lane, kend, BS);
     for (int j = 0; j < ntiles; ++j) {
       const int st = j % C::STAGES;
       const uint32_t ph = (uint32_t)(j / C::STAGES) & 1u;
-      if (!warp_wait(&kv_empty[st], ph ^ 1u, p.status, abort_flag)) break;
+      const int lp = j * C::PAGES;  // first local page of the tile
+      if ((lp >> 5) != chunk) {
+        chunk = lp >> 5;
+        const int64_t page = pg0 + chunk * 32 + lane;
+        const int raw = page < p.max_pages ? pt_row[page] : -1;
+        blk_lane = prefill_checked_block(p, raw, page, kend, BS);
+      }
+      if (!warp_wait(&empty[st], ph ^ 1u, p.status, abort_flag)) break;
       int blks[C::PAGES];
       uint32_t bytes = 0;
 #pragma unroll
       for (int pg = 0; pg < C::PAGES; ++pg) {
-        const int blk = sblk[j * C::PAGES + pg];
+        const int blk = __shfl_sync(kFullMask, blk_lane, (lp + pg) & 31);
         blks[pg] = blk;
         if (blk >= 0) {
-          bytes += 2u * BS * D * 2;
+          bytes += (uint32_t)(BS * D * 2);
         } else {
           // Pages that are not loaded must not hold stale or uninitialised
           // bytes: their softmax weight is 0, but 0 * NaN is NaN in P.V.
 #pragma unroll
           for (int kb = 0; kb < C::KB; ++kb) {
             const int off = st * C::KV_BYTES + kb * (C::BN * 128) + pg * (BS * 128);
-            for (int i = lane; i < BS * 8; i += 32) {
-              reinterpret_cast<uint4*>(sK + off)[i] = make_uint4(0, 0, 0, 0);
-              reinterpret_cast<uint4*>(sV + off)[i] = make_uint4(0, 0, 0, 0);
-            }
+            for (int i = lane; i < BS * 8; i += 32) reinterpret_cast<uint4*>(ring + off)[i] = make_uint4(0, 0, 0, 0);
           }
         }
       }
       tc::fence_proxy_async_smem();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive_expect_tx(&kv_full[st], bytes);
+        mbar_arrive_expect_tx(&full[st], bytes);
 #pragma unroll
         for (int pg = 0; pg < C::PAGES; ++pg) {
           if (blks[pg] < 0) continue;
@@ -255,101 +289,150 @@ __global__ void __launch_bounds__(192, PfTcCfg<D, BS>::MIN_BLOCKS)
 #pragma unroll
           for (int kb = 0; kb < C::KB; ++kb) {
             const int off = st * C::KV_BYTES + kb * (C::BN * 128) + pg * (BS * 128);
-            tc::tma_load_2d(sK + off, &tm_k, kb * 64, row, &kv_full[st]);
-            tc::tma_load_2d(sV + off, &tm_v, kb * 64, row, &kv_full[st]);
+            tc::tma_load_2d(ring + off, tmap, kb * 64, row, &full[st]);
           }
         }
       }
       __syncwarp();
     }
-  } else if (warp == 5) {
+  } else if (warp == C::MMA_WARP) {
     // ------------------------------------------------------------ MMA issue
-    // Order: QK(0), QK(1), then per tile j: PV(j) once P(j) is ready, then
-    // QK(j+2) into the S buffer tile j just released.  The softmax of tile
-    // j+1 therefore overlaps PV(j) and the load of tile j+2.
+    tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tc::tmem_relinquish();
+    tc::fence_before_sync();
+    named_bar_sync(1, C::THREADS);
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    // Order: Q.K^T(0 .. NSLOT-1), then per tile j: P.V(j) once P(j) is ready,
+    // then Q.K^T(j+NSLOT) into the S buffer tile j released.  Tile j uses S/P
+    // buffer j % NSLOT and the O accumulator of group j % NG.
     constexpr int FMT = sizeof(T) == 2 && ElemTraits<T>::kDtype == B2PA_DTYPE_BF16 ? 1 : 0;
     constexpr uint32_t idesc_s = tc::idesc_f16(128, C::BN, FMT, 0, 0);
     constexpr uint32_t idesc_o = tc::idesc_f16(128, D, FMT, 0, 1);
-    const uint32_t aQ = smem_u32(sQ), aK = smem_u32(sK), aV = smem_u32(sV), aP = smem_u32(sP);
+    // Descriptors of the operand bases; an operand at byte offset `off` from
+    // its base is base + off / 16 (the start-address field, which cannot
+    // carry: shared addresses stay below 2^18).
+    const uint64_t dQ = tc::smem_desc(smem_u32(sQ), 16, 1024);
+    const uint64_t dK = tc::smem_desc(smem_u32(sK), 16, 1024);
+    const uint64_t dV = tc::smem_desc(smem_u32(sV), C::BN * 128, 1024);
+    const uint64_t dP = tc::smem_desc(smem_u32(sP), 16, 1024);
     auto issue_qk = [&](int j) -> bool {
       const int st = j % C::STAGES;
-      if (!warp_wait(&kv_full[st], (uint32_t)(j / C::STAGES) & 1u, p.status, abort_flag)) return false;
+      if (!warp_wait(&k_full[st], (uint32_t)(j / C::STAGES) & 1u, p.status, abort_flag)) return false;
       tc::fence_after_sync();
       if (lane == 0) {
-        const uint32_t tS = tS0 + (uint32_t)(j & 1) * C::BN;
+        const uint32_t tS = tmem + (uint32_t)(j % NSLOT) * C::BN;
+        const uint64_t dKs = dK + (uint64_t)((st * C::KV_BYTES) >> 4);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           const int kb = k >> 2, kk = k & 3;
-          const uint64_t a = tc::smem_desc(aQ + kb * (C::BM * 128) + kk * 32, 16, 1024);
-          const uint64_t bd = tc::smem_desc(aK + st * C::KV_BYTES + kb * (C::BN * 128) + kk * 32, 16, 1024);
+          const uint64_t a = dQ + (uint64_t)((kb * (C::BM * 128) + kk * 32) >> 4);
+          const uint64_t bd = dKs + (uint64_t)((kb * (C::BN * 128) + kk * 32) >> 4);
           tc::mma_f16_ss(tS, a, bd, idesc_s, k > 0);
         }
-        tc::commit(&s_full[j & 1]);
+        tc::commit(&s_full[j % NSLOT]);
+        tc::commit(&k_empty[st]);
       }
       __syncwarp();
       return true;
     };
     bool ok = true;
-    if (ntiles > 0) ok = issue_qk(0);
-    if (ok && ntiles > 1) ok = issue_qk(1);
+    for (int j = 0; j < NSLOT && j < ntiles && ok; ++j) ok = issue_qk(j);
     for (int j = 0; j < ntiles && ok; ++j) {
       const int st = j % C::STAGES;
-      if (!warp_wait(&p_full[j & 1], (uint32_t)(j >> 1) & 1u, p.status, abort_flag)) break;
+      const int slot = j % NSLOT, g = j % NG;
+      if (!warp_wait(&p_full[slot], (uint32_t)(j / NSLOT) & 1u, p.status, abort_flag)) break;
+      if (!warp_wait(&v_full[st], (uint32_t)(j / C::STAGES) & 1u, p.status, abort_flag)) break;
       tc::fence_after_sync();
       if (lane == 0) {
-        const uint32_t aPj = aP + (uint32_t)(j & 1) * C::P_BYTES;
+        const uint64_t dPs = dP + (uint64_t)((slot * C::P_BYTES) >> 4);
+        const uint64_t dVs = dV + (uint64_t)((st * C::KV_BYTES) >> 4);
+        const uint32_t tO = tmem + (uint32_t)(NSLOT * C::BN + g * D);
 #pragma unroll
-        for (int k = 0; k < C::BN / 16; ++k) {
-          const uint64_t a = tc::smem_desc(aPj + k * 32, 16, 1024);
-          const uint64_t bd = tc::smem_desc(aV + st * C::KV_BYTES + k * 2048, C::BN * 128, 1024);
-          tc::mma_f16_ss(tO, a, bd, idesc_o, j > 0 || k > 0);
-        }
-        tc::commit(o_full);
-        tc::commit(&kv_empty[st]);
+        for (int k = 0; k < C::BN / 16; ++k)
+          tc::mma_f16_ss(tO, dPs + (uint64_t)(k * 2), dVs + (uint64_t)(k * 128), idesc_o, j >= NG || k > 0);
+        tc::commit(&o_full[g]);
+        tc::commit(&v_empty[st]);
       }
       __syncwarp();
-      if (j + 2 < ntiles) ok = issue_qk(j + 2);
+      if (j + NSLOT < ntiles) ok = issue_qk(j + NSLOT);
     }
-    // The epilogue cannot wait on o_full by parity: when it runs, only
-    // P.V(ntiles-3) is known complete, so o_full may still be two phases
-    // behind.  A separate single-phase barrier marks "all MMAs done".
+    // The epilogue cannot wait on o_full by parity (it may lag by two
+    // phases); a separate single-phase barrier marks "all MMAs done".
     if (ok && ntiles > 0 && lane == 0) tc::commit(o_final);
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax
-    const int r = tid;
+    const int g = warp >> 2;     // softmax group
+    const int r = tid & 127;     // query row (TMEM lane) of this thread
     const int t = t0 + r;
+    // Q rows -> 128B-swizzled K-major tile, zeros past T; consecutive
+    // threads read consecutive 16-byte pieces of a row.
+#pragma unroll
+    for (int it = 0; it < C::BM * D / 8 / C::SOFTMAX_THREADS; ++it) {
+      const int c = tid + it * C::SOFTMAX_THREADS;
+      const int qr = c / (D / 8), qc = c % (D / 8);
+      const int qt = t0 + qr;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (qt < p.T)
+        v = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + (int64_t)b * p.sq_b + (int64_t)h * p.sq_h +
+                                            (int64_t)qt * p.sq_t + qc * 8);
+      *reinterpret_cast<uint4*>(sQ + (qc >> 3) * (C::BM * 128) + tc::sw128_offset(qr, qc & 7)) = v;
+    }
+    tc::fence_proxy_async_smem();
+    tc::fence_before_sync();
+    named_bar_sync(1, C::THREADS);
+    tc::fence_after_sync();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tO = tmem + (uint32_t)(NSLOT * C::BN);  // O of group gg at tO + gg * D
+    // Block ids of the CTA's pages (for the visibility mask), validated once.
+    {
+      const int npg = ntiles * C::PAGES;
+      for (int i = tid; i < npg; i += C::SOFTMAX_THREADS) {
+        const int64_t page = pg0 + i;
+        const int raw = i == tid ? blk_pre : (page < p.max_pages ? pt_row[page] : -1);
+        sblk[i] = prefill_checked_block(p, raw, page, kend, BS);
+      }
+    }
+    named_bar_sync(2, C::SOFTMAX_THREADS);
     int64_t row_end = L < past + t + 1 ? L : past + t + 1;
     if (row_end > cap) row_end = cap;
-    const uint32_t trow = (uint32_t)(warp * 32) << 16;
+    const uint32_t trow = (uint32_t)((warp & 3) * 32) << 16;
     // O accumulates in TMEM at the scale 2^m_ref.  m_ref only moves when a
     // tile's row max exceeds it by more than kRescale (log2 units), so the
     // P values stay below 2^kRescale and the rescale of O (TMEM load, scale,
-    // store) is rare.  Rescaling at tile j waits for P.V(j-1): the o_full
-    // barrier completes one phase per P.V; S(j) being ready implies every MMA
-    // issued before QK(j) -- so P.V(j-2) -- is done, and P.V(j) cannot start
-    // before this warp releases P(j), so o_full is in phase j-1 or j and the
-    // parity wait is exact.
+    // store) is rare.  Rescaling at the group's i-th tile j waits for the
+    // group's previous P.V (tile j - NG): o_full[g] completes one phase per
+    // P.V of the group; S(j) being ready implies every MMA issued before
+    // Q.K^T(j) -- so P.V(j - 2*NG) -- is done, and P.V(j) cannot start
+    // before this warp releases P(j), so o_full[g] is in phase i-1 or i and
+    // the parity wait is exact.
     constexpr float kRescale = 8.f;
+    // Row maxima are taken on unscaled scores and scaled once (sc > 0); a
+    // scale that is not positive is applied to the scores first instead.
+    const bool pre_scale = !(p.scale_log2 > 0.f);
+    const float sc = pre_scale ? 1.f : p.scale_log2;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
-    for (int j = 0; j < ntiles; ++j) {
-      if (!warp_wait(&s_full[j & 1], (uint32_t)(j >> 1) & 1u, p.status, abort_flag)) {
+    for (int j = g; j < ntiles; j += NG) {
+      const int i = j / NG;
+      const int slot = j % NSLOT;
+      if (!warp_wait(&s_full[slot], (uint32_t)(j / NSLOT) & 1u, p.status, abort_flag)) {
         ok = false;
         break;
       }
       tc::fence_after_sync();
       float s[64];
+      const uint32_t tS = tmem + (uint32_t)slot * C::BN + trow;
       {
-        const uint32_t tS = tS0 + (uint32_t)(j & 1) * C::BN;
         float a[32], c[32];
-        tc::tmem_ld32(tS + trow, a);
-        tc::tmem_ld32(tS + trow + 32, c);
+        tc::tmem_ld32(tS, a);
+        tc::tmem_ld32(tS + 32, c);
         tc::tmem_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          s[i] = a[i];
-          s[32 + i] = c[i];
+        for (int e = 0; e < 32; ++e) {
+          s[e] = a[e];
+          s[32 + e] = c[e];
         }
       }
       const int64_t k0 = (int64_t)(j0 + j) * C::BN;
@@ -363,24 +446,27 @@ __global__ void __launch_bounds__(192, PfTcCfg<D, BS>::MIN_BLOCKS)
       // Keys of this tile visible to this row: [0, lim) (and pages present).
       const int64_t lim64 = row_end - k0;
       const int lim = lim64 < 0 ? 0 : (lim64 > C::BN ? C::BN : (int)lim64);
-      if (lim == C::BN && all_pages) {
+      // Scores stay unscaled (the scale enters the exponent's fma below)
+      // unless it is not positive; invisible keys become -inf.
+      if (pre_scale) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) s[i] *= p.scale_log2;
-      } else {
+        for (int e = 0; e < 64; ++e) s[e] *= p.scale_log2;
+      }
+      if (lim < C::BN || !all_pages) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) {
-          const bool vis = i < lim && page_ok[i / BS];
-          s[i] = vis ? s[i] * p.scale_log2 : -INFINITY;
+        for (int e = 0; e < 64; ++e) {
+          const bool vis = e < lim && page_ok[e / BS];
+          s[e] = vis ? s[e] : -INFINITY;
         }
       }
-      // Row max as a tree (short dependency chains: one warp per SM
-      // sub-partition runs this, so latency, not throughput, bounds it).
+      // Row max as a tree (short dependency chains).
       float mx[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = fmaxf(fmaxf(s[i], s[i + 8]), fmaxf(s[i + 16], s[i + 24]));
+      for (int e = 0; e < 8; ++e) mx[e] = fmaxf(fmaxf(s[e], s[e + 8]), fmaxf(s[e + 16], s[e + 24]));
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], fmaxf(fmaxf(s[i + 32], s[i + 40]), fmaxf(s[i + 48], s[i + 56])));
-      const float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], fmaxf(fmaxf(s[e + 32], s[e + 40]), fmaxf(s[e + 48], s[e + 56])));
+      const float mt =
+          sc * fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       // A row moves its reference max when the tile's max exceeds it by more
       // than kRescale.  Rows that already hold O at the old scale need O and
       // l multiplied by 2^(m_old - m_new); a row with no visible key so far
@@ -390,10 +476,10 @@ __global__ void __launch_bounds__(192, PfTcCfg<D, BS>::MIN_BLOCKS)
       const bool need = mt > m + kRescale;
       const float m_new = need ? mt : m;
       const bool scale_o = need && m != -INFINITY;
-      if (j > 0 && __any_sync(kFullMask, scale_o)) {
+      if (i > 0 && __any_sync(kFullMask, scale_o)) {
         const float alpha = scale_o ? fast_exp2(m - m_new) : 1.f;
-        // wait for P.V(j-1) before touching O
-        if (!warp_wait(o_full, (uint32_t)(j - 1) & 1u, p.status, abort_flag)) {
+        // wait for the group's previous P.V before touching its O
+        if (!warp_wait(&o_full[g], (uint32_t)(i - 1) & 1u, p.status, abort_flag)) {
           ok = false;
           break;
         }
@@ -401,64 +487,109 @@ __global__ void __launch_bounds__(192, PfTcCfg<D, BS>::MIN_BLOCKS)
 #pragma unroll
         for (int cb = 0; cb < D / 32; ++cb) {
           float ov[32];
-          tc::tmem_ld32(tO + trow + cb * 32, ov);
+          tc::tmem_ld32(tO + g * D + trow + cb * 32, ov);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) ov[i] *= alpha;
-          tc::tmem_st32(tO + trow + cb * 32, ov);
+          for (int e = 0; e < 32; ++e) ov[e] *= alpha;
+          tc::tmem_st32(tO + g * D + trow + cb * 32, ov);
         }
         tc::tmem_wait_st();
         l *= alpha;
       }
       m = m_new;
-      const bool live = m != -INFINITY;
-      float ls[8];  // 8 independent partial sums
+      // P = 2^(s * sc - m), two lanes per fma; a row with no visible key so
+      // far (m = -inf) has every s at -inf, so any finite offset gives 0.
+      const float2 sc2 = make_float2(sc, sc);
+      const float2 nm2 = make_float2(m == -INFINITY ? 0.f : -m, m == -INFINITY ? 0.f : -m);
+      float2 ls[4];  // 8 independent partial sums
 #pragma unroll
-      for (int e = 0; e < 8; ++e) ls[e] = 0.f;
-      unsigned char* sPj = sP + (j & 1) * C::P_BYTES;  // free: S(j) ready implies P.V(j-2) done
+      for (int e = 0; e < 4; ++e) ls[e] = make_float2(0.f, 0.f);
+      unsigned char* sPj = sP + slot * C::P_BYTES;  // free: S(j) ready implies P.V(j - NSLOT) done
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) {
         float pv[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          pv[e] = live ? fast_exp2(s[c8 * 8 + e] - m) : 0.f;
-          ls[e] += pv[e];
+        for (int e = 0; e < 4; ++e) {
+          const float2 x = fma2(make_float2(s[c8 * 8 + 2 * e], s[c8 * 8 + 2 * e + 1]), sc2, nm2);
+          pv[2 * e] = fast_exp2(x.x);
+          pv[2 * e + 1] = fast_exp2(x.y);
+          ls[e] = add2(ls[e], make_float2(pv[2 * e], pv[2 * e + 1]));
         }
         Vec<T, 8> w;
         w.from_float(pv);
         *reinterpret_cast<uint4*>(sPj + tc::sw128_offset(r, c8)) = w.w;
       }
-      l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
+      const float2 l01 = add2(ls[0], ls[1]), l23 = add2(ls[2], ls[3]);
+      l += (l01.x + l01.y) + (l23.x + l23.y);
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&p_full[j & 1]);
+      if (lane == 0) mbar_arrive(&p_full[slot]);
     }
-    float o[D];
+    // ---------------------------------------------------------- epilogue
+    // Merge the groups' (m, l, O) for this row: weights 2^(m_g - M).  Group g
+    // writes columns [g*D/NG, (g+1)*D/NG) of the row.
+    float M = m, wgt[NG];
+    wgt[0] = 1.f;
+    float lsum = l;
+    if constexpr (NG > 1) {
+      sML[(g * C::BM + r) * 2] = m;
+      sML[(g * C::BM + r) * 2 + 1] = l;
+      named_bar_sync(2, C::SOFTMAX_THREADS);
+      float mg[NG], lg[NG];
 #pragma unroll
-    for (int i = 0; i < D; ++i) o[i] = 0.f;
+      for (int gg = 0; gg < NG; ++gg) {
+        mg[gg] = sML[(gg * C::BM + r) * 2];
+        lg[gg] = sML[(gg * C::BM + r) * 2 + 1];
+      }
+      M = mg[0];
+#pragma unroll
+      for (int gg = 1; gg < NG; ++gg) M = fmaxf(M, mg[gg]);
+      lsum = 0.f;
+#pragma unroll
+      for (int gg = 0; gg < NG; ++gg) {
+        wgt[gg] = mg[gg] == -INFINITY ? 0.f : fast_exp2(mg[gg] - M);
+        lsum = fmaf(lg[gg], wgt[gg], lsum);
+      }
+    }
+    constexpr int DC = D / NG;  // columns this thread writes
+    const int c0 = g * DC;
+    float o[DC];
+#pragma unroll
+    for (int e = 0; e < DC; ++e) o[e] = 0.f;
     if (ok && ntiles > 0 && warp_wait(o_final, 0u, p.status, abort_flag)) {
       tc::fence_after_sync();
 #pragma unroll
-      for (int cb = 0; cb < D / 32; ++cb) tc::tmem_ld32(tO + trow + cb * 32, *reinterpret_cast<float(*)[32]>(o + cb * 32));
-      tc::tmem_wait_ld();
+      for (int gg = 0; gg < NG; ++gg) {
+        if (gg >= ntiles) break;  // group without tiles: its O was never written
+#pragma unroll
+        for (int cb = 0; cb < DC / 32; ++cb) {
+          float ov[32];
+          tc::tmem_ld32(tO + gg * D + trow + c0 + cb * 32, ov);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[cb * 32 + e] = NG > 1 ? fmaf(wgt[gg], ov[e], o[cb * 32 + e]) : ov[e];
+        }
+      }
     }
     tc::fence_before_sync();
     if (t < p.T && nsplit > 1) {
       const int64_t slot = (((int64_t)b * p.H + h) * p.T + t) * p.nsplit_max + split;
-      float4* po = reinterpret_cast<float4*>(p.part_o + slot * D);
+      float4* po = reinterpret_cast<float4*>(p.part_o + slot * D + c0);
 #pragma unroll
-      for (int c4 = 0; c4 < D / 4; ++c4) po[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
-      p.part_ml[2 * slot] = m;
-      p.part_ml[2 * slot + 1] = l;
+      for (int c4 = 0; c4 < DC / 4; ++c4) po[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
+      if (g == 0) {
+        p.part_ml[2 * slot] = M;
+        p.part_ml[2 * slot + 1] = lsum;
+      }
     } else if (t < p.T) {
-      const float den = fmaxf(l, 1e-9f);
-      T* orow = static_cast<T*>(p.out) + (int64_t)b * p.so_b + (int64_t)h * p.so_h + (int64_t)t * p.so_t;
+      const float inv = 1.f / fmaxf(lsum, 1e-9f);
+      T* orow = static_cast<T*>(p.out) + (int64_t)b * p.so_b + (int64_t)h * p.so_h + (int64_t)t * p.so_t + c0;
 #pragma unroll
-      for (int c8 = 0; c8 < D / 8; ++c8) {
+      for (int c8 = 0; c8 < DC / 8; ++c8) {
         float f[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = o[c8 * 8 + e] / den;
+        for (int e = 0; e < 8; ++e) f[e] = o[c8 * 8 + e] * inv;
         Vec<T, 8> w;
         w.from_float(f);
         *reinterpret_cast<uint4*>(orow + c8 * 8) = w.w;
@@ -467,9 +598,9 @@ __global__ void __launch_bounds__(192, PfTcCfg<D, BS>::MIN_BLOCKS)
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == C::MMA_WARP) {
     tc::fence_after_sync();
-    tc::tmem_dealloc(tmem, C::TMEM_COLS);
+    tc::tmem_dealloc(*tmem_slot, C::TMEM_COLS);
   }
 }
 
