@@ -8,9 +8,12 @@ per batch of request states is kept and patched in place: block lists only
 grow (a block appended when the write position crosses a block boundary,
 paged_kv.py:110-113) or are cleared on release (:122-126), so each call only
 compares every row's list identity and length with the last snapshot and
-copies the new tail of the rows that changed.  The device table is uploaded
-again only when a row changed; the lengths (which change every step) and any
-per-call rows go up in one small pinned copy.
+copies the new tail of the rows that changed.  The device table stays
+resident: the cells that changed (one per sequence that crossed a block
+boundary, in decode) go up as (index, value) pairs together with the lengths
+(which change every step) and any per-call rows in one small pinned copy, and
+b2pa_patch_table writes them in place; only a table that had to grow, or a
+change of more than _MAX_PATCH_PAIRS cells, is uploaded whole.
 
 A batch is identified by the identity of its state objects and the current
 stream (uploads are ordered on that stream only; the reference
@@ -26,9 +29,13 @@ from collections import OrderedDict
 import numpy as np
 import torch
 
+from . import _lib
 from ._staging import stage_int32
 
 _MAX_ENTRIES = 64
+# Up to this many changed cells the resident device table is patched in place
+# (b2pa_patch_table); beyond it the whole table is uploaded again.
+_MAX_PATCH_PAIRS = 1 << 16
 
 
 class _Entry:
@@ -48,16 +55,20 @@ class _Entry:
 _entries: "OrderedDict[tuple, _Entry]" = OrderedDict()
 
 
-def _refresh_rows(ent: _Entry, seq_out: np.ndarray | None = None, states=None) -> tuple[bool, int]:
+def _refresh_rows(ent: _Entry, seq_out: np.ndarray | None = None, states=None,
+                  cells: list | None = None) -> tuple[bool, int]:
     """Brings the host table up to date in one pass over the states; returns
     (any row changed, max block count) and fills ``seq_out`` with seq_len.
     A max block count of -1 asks the caller to rebuild the entry (a row
-    outgrew the table, or ``states`` no longer holds the entry's states)."""
+    outgrew the table, or ``states`` no longer holds the entry's states).
+    With ``cells`` (a list), the flat index and new value of every table
+    cell that changed are appended to it, interleaved."""
     changed = False
     table = ent.table
     counts = ent.counts
     lists = ent.lists
     mine = ent.states
+    width = ent.width
     if states is not None and len(states) != len(mine):
         return True, -1
     max_pages = 0
@@ -73,14 +84,24 @@ def _refresh_rows(ent: _Entry, seq_out: np.ndarray | None = None, states=None) -
         old = counts[r]
         if n == old and ids is lists[r]:
             continue
-        if n > ent.width:
+        if n > width:
             return True, -1  # caller rebuilds a wider table
         if ids is lists[r] and n > old:
             table[r, old:n] = ids[old:n]
+            if cells is not None:
+                base = r * width
+                for c in range(old, n):
+                    cells.append(base + c)
+                    cells.append(ids[c])
         else:
             table[r, :n] = ids
             if n < old:
                 table[r, n:old] = -1
+            if cells is not None:
+                base = r * width
+                for c in range(max(n, old)):
+                    cells.append(base + c)
+                    cells.append(ids[c] if c < n else -1)
         lists[r] = ids
         counts[r] = n
         changed = True
@@ -110,7 +131,8 @@ def block_table_and_lengths(cache, device: torch.device, extra: list[list[int]] 
     rows = 1 + (len(extra) if extra else 0)
     small = np.empty(B * rows, dtype=np.int32)
     ent = _lookup(cache, device, stream)
-    changed, max_pages = (True, -1) if ent is None else _refresh_rows(ent, small, states)
+    cells: list | None = [] if ent is not None and ent.dev_table is not None else None
+    changed, max_pages = (True, -1) if ent is None else _refresh_rows(ent, small, states, cells)
     if max_pages < 0:
         max_pages = max((len(s.block_ids) for s in states), default=0)
         width = max(max_pages, 1)
@@ -121,17 +143,27 @@ def block_table_and_lengths(cache, device: torch.device, extra: list[list[int]] 
         _entries[key] = ent
         while len(_entries) > _MAX_ENTRIES:
             _entries.popitem(last=False)
+        cells = None
         changed, max_pages = _refresh_rows(ent, small)
     ent.states_ref = states
     try:
         cache._b2pa_meta = ((device.index, stream), ent)
     except AttributeError:  # batch objects that refuse new attributes use the LRU only
         pass
-    dirty = changed or ent.dev_table is None
     if extra:
         for i, row in enumerate(extra):
             small[B * (i + 1): B * (i + 2)] = row
-    if dirty:
+    n_pairs = len(cells) // 2 if cells is not None else 0
+    if ent.dev_table is not None and changed and 0 < n_pairs <= _MAX_PATCH_PAIRS:
+        # few cells changed: send (index, value) pairs with the small rows and
+        # patch the resident table in place
+        packed = np.concatenate([small, np.asarray(cells, dtype=np.int32)])
+        dev = stage_int32(packed, device)
+        tail = dev[: B * rows]
+        lib = _lib.load()
+        _lib.check(lib.b2pa_patch_table(ent.dev_table.data_ptr(), ent.dev_table.numel(), dev[B * rows:].data_ptr(),
+                                        n_pairs, _lib.status_buffer(device).data_ptr(), stream), "b2pa_patch_table")
+    elif changed or ent.dev_table is None:
         packed = np.concatenate([ent.table.reshape(-1), small])
         dev = stage_int32(packed, device)
         ent.dev_table = dev[: B * ent.width].view(B, ent.width)

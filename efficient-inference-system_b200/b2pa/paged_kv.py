@@ -21,7 +21,9 @@ CPU pools are rejected -- there is no CPU path in this package.
 from __future__ import annotations
 
 import ctypes
+import itertools
 import math
+import operator
 from dataclasses import dataclass, field
 
 import numpy as np
@@ -235,33 +237,45 @@ def reserve_tokens(state, length: int) -> int:
     return start
 
 
-def plan_append(cache, k_new: torch.Tensor, lengths: list[int]) -> list[int]:
+_seq_len_of = operator.attrgetter("seq_len")
+_pool_of = operator.attrgetter("pool")
+
+
+def plan_append(cache, k_new: torch.Tensor, lengths) -> list[int]:
     """Initialises the pool and allocates blocks request by request, in batch
-    order (paged_kv.py:165-171); returns each request's start position."""
+    order (paged_kv.py:165-171); returns each request's start position.
+
+    The per-request arithmetic is vectorised; only requests whose write
+    crosses into new blocks (one in ``block_size`` per decode step) run the
+    allocation loop, still in batch order, so the LIFO free list hands out
+    the same ids as the reference's loop."""
     _, H, T, D = k_new.shape
     pool = cache.pool
-    if any(n > 0 for n in lengths):
+    states = cache.states
+    n = np.clip(np.asarray(lengths, dtype=np.int64), 0, T)
+    if n.any():
         pool.ensure_initialized(H, D, k_new.dtype, k_new.device)
+    if not all(map(operator.is_, map(_pool_of, states), itertools.repeat(pool))):
+        raise ValueError("b2pa: all states of a BatchedPagedKVCache must share its pool")
+    start = np.fromiter(map(_seq_len_of, states), dtype=np.int64, count=len(states))
     bs = pool.block_size
+    # one block each time the write position reaches a block boundary
+    # (paged_kv.py:110-113): blocks for positions start .. start+n-1
+    need = np.where(n > 0, (start + n + bs - 1) // bs - (start + bs - 1) // bs, 0)
     allocate = pool.allocate_block
-    starts = []
-    for b, state in enumerate(cache.states):
-        if state.pool is not pool:
-            raise ValueError("b2pa: all states of a BatchedPagedKVCache must share its pool")
-        start = state.seq_len
-        starts.append(start)
-        n = lengths[b]
-        n = T if n > T else (0 if n < 0 else n)
-        if n <= 0:
-            continue
-        # one block each time the write position reaches a block boundary
-        # (paged_kv.py:110-113): blocks for positions start .. start+n-1
-        need = (start + n + bs - 1) // bs - (start + bs - 1) // bs
-        ids = state.block_ids
-        for _ in range(need):
+    for b in np.flatnonzero(need).tolist():
+        ids = states[b].block_ids
+        for _ in range(int(need[b])):
             ids.append(allocate())
-        state.seq_len = start + n
-    return starts
+    grown = np.flatnonzero(n)
+    if len(grown) == len(states):
+        for state, length in zip(states, (start + n).tolist()):
+            state.seq_len = length
+    else:
+        ends = (start + n).tolist()
+        for b in grown.tolist():
+            states[b].seq_len = ends[b]
+    return start.tolist()
 
 
 def append_batch_into(cache, k_new: torch.Tensor, v_new: torch.Tensor, current_lengths=None) -> torch.Tensor:
@@ -273,11 +287,12 @@ def append_batch_into(cache, k_new: torch.Tensor, v_new: torch.Tensor, current_l
     if v_new.shape != k_new.shape or v_new.dtype != k_new.dtype:
         raise ValueError("k_new and v_new must have the same shape and dtype")
     lengths = host_lengths(current_lengths, T, B)
-    clamped = [max(min(n, T), 0) for n in lengths]
-    if any(clamped) and k_new.device.type not in ("cuda", "meta"):
+    clamped = np.clip(np.asarray(lengths, dtype=np.int64), 0, T)
+    any_new = bool(clamped.any())
+    if any_new and k_new.device.type not in ("cuda", "meta"):
         raise RuntimeError("b2pa: k_new must be a CUDA tensor (this package has no CPU path)")
     starts = plan_append(cache, k_new, clamped)
-    if any(clamped) and k_new.device.type == "cuda":
+    if any_new and k_new.device.type == "cuda":
         seq_lens = _kv_append(cache, k_new, v_new, starts, clamped)
         return seq_lens.to(torch.long)
     return torch.tensor([s.seq_len for s in cache.states], dtype=torch.long, device=k_new.device)

@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdarg>
+#include <cstdint>
 #include <cstdio>
 #include <cstring>
 #include <map>
@@ -405,6 +406,15 @@ int b2pa_zero_blocks(void* k_pool, void* v_pool, const int64_t pool_strides[4], 
   a.dtype = dtype;
   a.status = status;
   return launch_zero_blocks(a, static_cast<cudaStream_t>(stream));
+}
+
+int b2pa_patch_table(int32_t* table, int64_t n_cells, const int32_t* pairs, int n_pairs, int32_t* status,
+                     void* stream) {
+  if (n_pairs < 0 || n_cells < 0) return set_error(B2PA_ERR_INVALID_ARGUMENT, "patch_table: bad sizes");
+  if (n_pairs == 0) return B2PA_OK;
+  if (!table || !pairs) return set_error(B2PA_ERR_INVALID_ARGUMENT, "patch_table: null pointer argument");
+  if (n_cells > INT32_MAX) return set_error(B2PA_ERR_UNSUPPORTED, "patch_table: more than 2^31 cells");
+  return launch_patch_table(table, n_cells, pairs, n_pairs, status, static_cast<cudaStream_t>(stream));
 }
 
 }  // extern "C"

@@ -75,6 +75,8 @@ struct AttnArgs {
 
 int launch_kv_append(const AppendArgs& a, cudaStream_t stream);
 int launch_zero_blocks(const ZeroArgs& a, cudaStream_t stream);
+int launch_patch_table(int32_t* table, int64_t n_cells, const int32_t* pairs, int n_pairs, int32_t* status,
+                       cudaStream_t stream);
 
 // Decode planning shared by the workspace query and the launcher.
 struct DecodePlan {

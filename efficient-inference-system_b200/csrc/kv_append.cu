@@ -159,4 +159,26 @@ int launch_zero_blocks(const ZeroArgs& a, cudaStream_t stream) {
   return B2PA_OK;
 }
 
+// One thread per (index, value) pair of a block-table patch.
+__global__ void __launch_bounds__(256) patch_table_kernel(int32_t* table, int64_t n_cells, const int32_t* pairs,
+                                                          int n_pairs, int32_t* status) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n_pairs) return;
+  const int32_t idx = pairs[2 * i];
+  if (idx < 0 || (int64_t)idx >= n_cells) {
+    set_status(status, B2PA_ERR_INVALID_ARGUMENT);
+    return;
+  }
+  table[idx] = pairs[2 * i + 1];
+}
+
+int launch_patch_table(int32_t* table, int64_t n_cells, const int32_t* pairs, int n_pairs, int32_t* status,
+                       cudaStream_t stream) {
+  if (n_pairs == 0) return B2PA_OK;
+  patch_table_kernel<<<(n_pairs + 255) / 256, 256, 0, stream>>>(table, n_cells, pairs, n_pairs, status);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "patch_table launch: %s", cudaGetErrorString(e));
+  return B2PA_OK;
+}
+
 }  // namespace b2pa

@@ -188,6 +188,19 @@ B2PA_API int b2pa_zero_blocks(void* k_pool, void* v_pool, const int64_t pool_str
                      int H, int D, int block_size, int dtype,
                      int32_t* status, void* stream);
 
+/*
+ * Writes table[pairs[2i]] = pairs[2i+1] for i < n_pairs: an in-place update
+ * of a device-resident int32 block table (or any int32 array of n_cells
+ * entries).  No reference counterpart: the reference rebuilds the whole
+ * [B, max_pages] table from Python lists and copies it to the device on every
+ * call (BatchedPagedKVCache.page_table_tensor, src/cache/paged_kv.py:174-193);
+ * this lets the caller keep the table resident and send only the cells that
+ * changed.  An index outside [0, n_cells) is skipped and recorded as
+ * B2PA_ERR_INVALID_ARGUMENT in *status.
+ */
+B2PA_API int b2pa_patch_table(int32_t* table, int64_t n_cells, const int32_t* pairs, int n_pairs,
+                     int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -119,3 +119,48 @@ def test_bad_block_id_is_reported_not_faulted(cuda_device):
     b2pa.clear_status(cuda_device)
     assert k_pool.abs().sum().item() == 0
     del ctypes
+
+
+def test_patch_table_writes_cells_and_reports_bad_index(cuda_device):
+    """b2pa_patch_table writes each (index, value) pair; an index outside the
+    table is skipped and flagged, the others still land."""
+    from b2pa import _lib
+
+    lib = b2pa.load_library()
+    table = torch.full((4, 8), -1, dtype=torch.int32, device=cuda_device)
+    pairs = torch.tensor([0, 5, 9, 7, 31, 2, 32, 99, -1, 4], dtype=torch.int32, device=cuda_device)
+    b2pa.clear_status(cuda_device)
+    rc = lib.b2pa_patch_table(table.data_ptr(), table.numel(), pairs.data_ptr(), 5,
+                              _lib.status_buffer(cuda_device).data_ptr(), _lib.stream_handle(cuda_device))
+    assert rc == 0
+    want = np.full(32, -1, dtype=np.int32)
+    want[0], want[9], want[31] = 5, 7, 2
+    assert np.array_equal(table.cpu().numpy().reshape(-1), want)
+    assert b2pa.read_status(cuda_device) == -1
+    b2pa.clear_status(cuda_device)
+
+
+def test_resident_table_patched_across_steps(cuda_device):
+    """Many decode-style steps on one batch (the device table is patched in
+    place, never re-uploaded whole): the device table equals the reference's
+    page table after every step, including after a release and regrowth."""
+    from b2pa.paged_kv import device_metadata
+
+    pool = b2pa.LayerBlockPool(16, 64, 2.0)
+    rng = np.random.default_rng(11)
+    states = [b2pa.PagedKVCacheState(pool=pool) for _ in range(5)]
+    cache = b2pa.BatchedPagedKVCache(states, pool=pool)
+    k = torch.randn(5, 2, 40, 32, device=cuda_device)
+    cache.append_batch(k, k, [int(x) for x in rng.integers(1, 40, size=5)])
+    for step in range(60):
+        one = torch.randn(5, 2, 1, 32, device=cuda_device)
+        cache.append_batch(one, one, 1)
+        if step == 30:
+            states[2].release()
+        table, seq_lens, max_pages = device_metadata(cache, torch.device(cuda_device))
+        want = cache.page_table_array()
+        got = table.cpu().numpy()
+        assert np.array_equal(got[:, :want.shape[1]], want)
+        assert (got[:, want.shape[1]:] == -1).all()
+        assert seq_lens.cpu().tolist() == [s.seq_len for s in states]
+    assert b2pa.read_status(cuda_device) == 0
