@@ -170,6 +170,33 @@ def run_device_steps(torch, lib, _lib, wl: Workload, dev, first_step: int, n: in
             decode_events[i][1].record(stream)
 
 
+def count_step_launches(torch, lib, _lib, wl: Workload, dev, step: int):
+    """Kernels one device step launches, counted from a captured (never
+    replayed) CUDA graph of that step: its kernel nodes.  None if the graph
+    API is unavailable."""
+    try:
+        from cuda.bindings import runtime as cudart
+    except ImportError:
+        return None
+    g = torch.cuda.CUDAGraph(keep_graph=True)
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            run_device_steps(torch, lib, _lib, wl, dev, step, 1)
+    err, _, n = cudart.cudaGraphGetNodes(g.raw_cuda_graph(), 0)
+    if err != cudart.cudaError_t.cudaSuccess:
+        return None
+    err, nodes, n = cudart.cudaGraphGetNodes(g.raw_cuda_graph(), n)
+    kernels = 0
+    for node in nodes[:n]:
+        err, kind = cudart.cudaGraphNodeGetType(node)
+        if err == cudart.cudaError_t.cudaSuccess and kind == cudart.cudaGraphNodeType.cudaGraphNodeTypeKernel:
+            kernels += 1
+    del g
+    return kernels
+
+
 def build_public_cache(b2pa, wl: Workload, lens_now: np.ndarray):
     """A b2pa BatchedPagedKVCache over the workload's pool, as the allocator
     would have left it at lengths ``lens_now``."""
@@ -336,6 +363,8 @@ def main(argv=None) -> int:
 
     # ---------------------------------------------- device-resident (value)
     run_device_steps(torch, lib, _lib, wl, dev, 0, args.warmup)
+    torch.cuda.synchronize(dev)
+    launches_per_step = count_step_launches(torch, lib, _lib, wl, dev, args.warmup)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
@@ -432,7 +461,7 @@ def main(argv=None) -> int:
         "hbm_gb_per_s_decode": achieved_gbs,
         "roofline": {
             "bound": "hbm",
-            "kernel": "paged_decode (plan + main + combine launches of one b2pa_paged_decode call)",
+            "kernel": "paged_decode (every launch of one b2pa_paged_decode call: the decode kernel and, when a sequence is split, the combine)",
             "achieved": achieved_gbs,
             "peak": peaks["hbm_gbs"],
             "peak_source": peaks["source"],
@@ -451,7 +480,8 @@ def main(argv=None) -> int:
             "d2h_bytes_per_step": B * H * D * 2,
             "path": "b2pa.BatchedPagedKVCache.append_batch + b2pa.paged_attention, pinned host inputs",
         },
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": (launches_per_step * args.steps) if launches_per_step is not None else None,
+        "gpu_launches_per_step": launches_per_step,
         "clocks": clock_info,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

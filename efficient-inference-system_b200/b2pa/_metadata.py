@@ -135,7 +135,9 @@ def block_table_and_lengths(cache, device: torch.device, extra: list[list[int]] 
     changed, max_pages = (True, -1) if ent is None else _refresh_rows(ent, small, states, cells)
     if max_pages < 0:
         max_pages = max((len(s.block_ids) for s in states), default=0)
-        width = max(max_pages, 1)
+        # headroom so that growing sequences do not force a rebuild (and a
+        # whole-table upload) every few steps
+        width = max(max_pages + max_pages // 8 + 8, 1)
         if ent is not None:
             width = max(width, ent.width * 2)
         ent = _Entry(states, width)

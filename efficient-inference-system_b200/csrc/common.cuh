@@ -203,6 +203,15 @@ __device__ __forceinline__ float2 add2(float2 a, float2 b) {
   return f2_from_bits(d);
 }
 
+// Programmatic dependent launch: a kernel launched with programmatic stream
+// serialization may start while its predecessor in the stream is still
+// running.  pdl_wait() returns once the predecessor grid has completed and
+// its memory is visible (a no-op for a normal launch); every kernel below
+// calls it before touching memory an earlier kernel may write.
+// pdl_launch_dependents() lets the successor start launching early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ------------------------------------------------------------ warp utils ---
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll

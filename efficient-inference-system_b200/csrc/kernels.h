@@ -23,6 +23,25 @@ int set_max_dynamic_smem_cached(const void* func, int bytes);
 // Multiprocessor count of the current device (cached per device).
 int device_sm_count();
 
+// Launches `kern` with programmatic stream serialization: it may begin while
+// the previous kernel in `stream` is still running and must call pdl_wait()
+// (common.cuh) before reading that kernel's results.  Host-only helper.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                       Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // Largest dynamic shared memory per block on the current device (opt-in).
 int device_max_smem_optin();
 

@@ -21,6 +21,8 @@ namespace b2pa {
 template <int VB>
 __global__ void __launch_bounds__(128) kv_append_kernel(AppendArgs a, int es) {
   using W = typename VecWord<VB>::type;
+  pdl_wait();
+  pdl_launch_dependents();
   const int t = blockIdx.x;
   const int b = blockIdx.y;
   int len = a.lengths[b];
@@ -60,6 +62,8 @@ __global__ void __launch_bounds__(128) kv_append_kernel(AppendArgs a, int es) {
 
 // Element-sized copy for 2-byte types whose strides rule out wider words.
 __global__ void __launch_bounds__(128) kv_append_kernel_u16(AppendArgs a) {
+  pdl_wait();
+  pdl_launch_dependents();
   const int t = blockIdx.x;
   const int b = blockIdx.y;
   int len = a.lengths[b];
@@ -131,12 +135,12 @@ int launch_kv_append(const AppendArgs& a, cudaStream_t stream) {
   dim3 grid(a.T, a.B);
   if (vb >= 4 && ok(vb)) {
     switch (vb) {
-      case 16: kv_append_kernel<16><<<grid, 128, 0, stream>>>(a, es); break;
-      case 8: kv_append_kernel<8><<<grid, 128, 0, stream>>>(a, es); break;
-      default: kv_append_kernel<4><<<grid, 128, 0, stream>>>(a, es); break;
+      case 16: launch_pdl(kv_append_kernel<16>, grid, dim3(128), 0, stream, a, es); break;
+      case 8: launch_pdl(kv_append_kernel<8>, grid, dim3(128), 0, stream, a, es); break;
+      default: launch_pdl(kv_append_kernel<4>, grid, dim3(128), 0, stream, a, es); break;
     }
   } else if (es == 2) {
-    kv_append_kernel_u16<<<grid, 128, 0, stream>>>(a);
+    launch_pdl(kv_append_kernel_u16, grid, dim3(128), 0, stream, a);
   } else {
     // fp32 with a non-unit D stride: the rows cannot be moved as words.
     return set_error(B2PA_ERR_UNSUPPORTED, "kv_append: fp32 tensors need a unit D stride");

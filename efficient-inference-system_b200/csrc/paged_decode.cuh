@@ -92,6 +92,8 @@ struct DecodeParams {
   int q_off;     // offset of the fp32 query block inside a stage
   float qscale;  // scale * log2(e)
   int32_t* item_off;
+  int plan_in_smem;  // 1: every CTA computes the item offsets itself (shared memory)
+  int off_smem;      // byte offset of those offsets in dynamic shared memory
   float* part_ml;
   float* part_acc;
   int32_t* status;
@@ -167,6 +169,59 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(DecodeParams p) {
   if (tid == 0) p.item_off[p.B] = carry;
 }
 
+// Items of sequence b: HG * number of splits (at least one split).
+template <int BS>
+__device__ __forceinline__ int decode_items_of(const DecodeParams& p, int b) {
+  const int vis = decode_visible(p, b, BS);
+  const int np = (vis + BS - 1) / BS;
+  const int ns = (np + p.pages_per_split - 1) / p.pages_per_split;
+  return (ns < 1 ? 1 : ns) * p.HG;
+}
+
+// The plan of decode_plan_kernel computed by one CTA of the decode kernel
+// (all its threads): off[b] = exclusive prefix of the item counts, off[B] =
+// total.  CTA 0 also publishes it to p.item_off for the combine kernel and
+// reports lengths past the page table.
+template <int BS>
+__device__ void decode_plan_cta(const DecodeParams& p, int* off) {
+  __shared__ int warp_tot[32];
+  const int nt = blockDim.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, nw = nt >> 5;
+  int carry = 0;
+  for (int base = 0; base < p.B; base += nt) {
+    const int b = base + tid;
+    int n = 0;
+    if (b < p.B) {
+      n = decode_items_of<BS>(p, b);
+      if (blockIdx.x == 0 && (int64_t)p.seq_lens[b] > (int64_t)p.max_pages * BS) set_status(p.status, B2PA_ERR_BAD_BLOCK_ID);
+    }
+    int x = n;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(kFullMask, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_tot[warp] = x;
+    __syncthreads();
+    int before = 0, all = 0;
+    for (int w2 = 0; w2 < nw; ++w2) {
+      const int t = warp_tot[w2];
+      before += w2 < warp ? t : 0;
+      all += t;
+    }
+    if (b < p.B) {
+      off[b] = carry + before + x - n;
+      if (blockIdx.x == 0) p.item_off[b] = carry + before + x - n;
+    }
+    carry += all;
+    __syncthreads();
+  }
+  if (tid == 0) {
+    off[p.B] = carry;
+    if (blockIdx.x == 0) p.item_off[p.B] = carry;
+  }
+  __syncthreads();
+}
+
 // Reduces v[0..N) over the M lanes (xor masks M/2..1) of a lane group so
 // that lane c ends up with the full sum of element (c >> (log2 M - log2 N)).
 template <int N, int M>
@@ -212,9 +267,19 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
     }
     fence_mbar_init();
   }
-  __syncthreads();
+  // Launched programmatically after the KV append: nothing below may read
+  // the pools (or anything else an earlier kernel writes) before this.
+  pdl_wait();
+  const int* off = p.item_off;
+  if (p.plan_in_smem) {
+    int* s_off = reinterpret_cast<int*>(smem + p.off_smem);
+    decode_plan_cta<BS>(p, s_off);  // ends with __syncthreads
+    off = s_off;
+  } else {
+    __syncthreads();
+  }
 
-  const int total = p.item_off[p.B];
+  const int total = off[p.B];
   const int chunk_bytes = G * Tile::HEAD_PAGE_BYTES;
 
   if (warp == G) {
@@ -228,7 +293,7 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
       // Locate the sequence of item w (items are visited in increasing order).
       while (true) {
         const int idx = cur_b + 1 + lane;
-        const int v = idx <= p.B ? p.item_off[idx] : INT_MAX;
+        const int v = idx <= p.B ? off[idx] : INT_MAX;
         const unsigned m = __ballot_sync(kFullMask, v > w);
         if (m) {
           cur_b += __ffs(m) - 1;
@@ -237,8 +302,8 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
         cur_b += 32;
       }
       const int b = cur_b;
-      const int off0 = p.item_off[b];
-      const int nsplit = (p.item_off[b + 1] - off0) / p.HG;
+      const int off0 = off[b];
+      const int nsplit = (off[b + 1] - off0) / p.HG;
       const int r = w - off0;
       const int hg = r / nsplit;
       const int s = r - hg * nsplit;
@@ -319,6 +384,7 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
         }
       }
     }
+    pdl_launch_dependents();
     if (!ok && lane == 0) {
       // Gave up: let every copy this CTA started land before exiting.
       for (int s2 = 0; s2 < p.stages; ++s2)
@@ -452,8 +518,12 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
 }
 
 // One warp per (sequence, head) whose sequence was split: log-sum-exp merge.
+// The split statistics are read one split per lane and reduced across the
+// warp, and the partial accumulators are read with independent loads (the
+// weights come by shuffle), so the merge is not a chain of dependent loads.
 template <typename T, int D>
 __global__ void __launch_bounds__(256) decode_combine_kernel(DecodeParams p) {
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t gw = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
   if (gw >= (int64_t)p.B * p.H) return;
@@ -466,24 +536,35 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(DecodeParams p) {
   const int hi = h - hg * p.G;
   const int64_t base = (int64_t)off0 + (int64_t)hg * nsplit;
   float M = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, p.part_ml[2 * ((base + s) * p.G + hi)]);
+  for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, p.part_ml[2 * ((base + s) * p.G + hi)]);
+  M = warp_max(M);
   constexpr int PER = D >= 32 ? D / 32 : 1;
   float o[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) o[i] = 0.f;
   float L = 0.f;
-  for (int s = 0; s < nsplit; ++s) {
-    const int64_t slot = (base + s) * p.G + hi;
-    const float ms = p.part_ml[2 * slot];
-    const float wgt = (M == -INFINITY) ? 0.f : exp2f(ms - M);
-    L = fmaf(p.part_ml[2 * slot + 1], wgt, L);
-    const float* pa = p.part_acc + slot * D;
+  for (int s0 = 0; s0 < nsplit; s0 += 32) {
+    const int s = s0 + lane;
+    float wl = 0.f;
+    if (s < nsplit) {
+      const int64_t slot = (base + s) * p.G + hi;
+      const float ms = p.part_ml[2 * slot];
+      wl = (M == -INFINITY) ? 0.f : exp2f(ms - M);
+      L = fmaf(p.part_ml[2 * slot + 1], wl, L);
+    }
+    const int cnt = nsplit - s0 < 32 ? nsplit - s0 : 32;
+#pragma unroll 4
+    for (int j = 0; j < cnt; ++j) {
+      const float wgt = __shfl_sync(kFullMask, wl, j);
+      const float* pa = p.part_acc + ((base + s0 + j) * p.G + hi) * D;
 #pragma unroll
-    for (int i = 0; i < PER; ++i) {
-      const int d = lane + 32 * i;
-      if (d < D) o[i] = fmaf(wgt, pa[d], o[i]);
+      for (int i = 0; i < PER; ++i) {
+        const int d = lane + 32 * i;
+        if (d < D) o[i] = fmaf(wgt, pa[d], o[i]);
+      }
     }
   }
+  L = warp_sum(L);
   const float den = fmaxf(L, 1e-9f);
   T* out = static_cast<T*>(p.out) + (int64_t)b * p.so_b + (int64_t)h * p.so_h;
 #pragma unroll
@@ -534,7 +615,12 @@ int launch_decode_impl(const AttnArgs& a, const DecodePlan& plan, cudaStream_t s
   const int max_smem = device_max_smem_optin();
   while (stages > 2 && (size_t)stages * p.stage_bytes + 16 * stages > (size_t)max_smem) --stages;
   p.stages = stages;
-  const size_t smem = (size_t)stages * p.stage_bytes + 16 * stages;
+  // Item offsets in shared memory (every CTA computes them) when they fit;
+  // otherwise the one-CTA plan kernel writes them to the workspace.
+  p.off_smem = stages * p.stage_bytes + 16 * stages;
+  const size_t off_bytes = ((size_t)(a.B + 1) * 4 + 15) / 16 * 16;
+  p.plan_in_smem = off_bytes <= 32 * 1024 && (size_t)p.off_smem + off_bytes <= (size_t)max_smem ? 1 : 0;
+  const size_t smem = (size_t)p.off_smem + (p.plan_in_smem ? off_bytes : 0);
   if (smem > (size_t)max_smem)
     return set_error(B2PA_ERR_UNSUPPORTED, "paged_decode: %zu bytes of shared memory exceed the device limit", smem);
   const int threads = (plan.G + 1) * 32;
@@ -549,11 +635,15 @@ int launch_decode_impl(const AttnArgs& a, const DecodePlan& plan, cudaStream_t s
   if (grid > plan.max_items) grid = plan.max_items;
   if (grid < 1) grid = 1;
 
-  decode_plan_kernel<BS><<<1, 1024, 0, stream>>>(p);
-  kern<<<(unsigned)grid, threads, smem, stream>>>(p);
-  const int64_t warps = (int64_t)a.B * a.H;
-  const unsigned cgrid = (unsigned)((warps + 7) / 8);
-  decode_combine_kernel<T, D><<<cgrid, 256, 0, stream>>>(p);
+  if (!p.plan_in_smem) decode_plan_kernel<BS><<<1, 1024, 0, stream>>>(p);
+  e = launch_pdl(kern, dim3((unsigned)grid), dim3(threads), smem, stream, p);
+  if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_decode launch: %s", cudaGetErrorString(e));
+  if (plan.max_items > (int64_t)a.B * plan.HG) {  // some sequence may be split
+    const int64_t warps = (int64_t)a.B * a.H;
+    const unsigned cgrid = (unsigned)((warps + 7) / 8);
+    e = launch_pdl(decode_combine_kernel<T, D>, dim3(cgrid), dim3(256), 0, stream, p);
+    if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_decode combine launch: %s", cudaGetErrorString(e));
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_decode launch: %s", cudaGetErrorString(e));
   return B2PA_OK;
