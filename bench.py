@@ -182,6 +182,10 @@ def count_step_launches(torch, lib, _lib, wl: Workload, dev, step: int):
     s = torch.cuda.Stream(dev)
     s.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(s):
+        # the capture stream's workspace exists before capture (an allocation
+        # inside the graph would add nodes that are not this step's kernels)
+        _lib.workspace(dev, lib.b2pa_paged_decode_workspace_size(wl.B, H, D, wl.max_pages, BS, _lib.DTYPE_BF16))
+        torch.cuda.synchronize(dev)
         with torch.cuda.graph(g, stream=s):
             run_device_steps(torch, lib, _lib, wl, dev, step, 1)
     err, _, n = cudart.cudaGraphGetNodes(g.raw_cuda_graph(), 0)

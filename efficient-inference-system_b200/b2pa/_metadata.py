@@ -8,7 +8,10 @@ per batch of request states is kept and patched in place: block lists only
 grow (a block appended when the write position crosses a block boundary,
 paged_kv.py:110-113) or are cleared on release (:122-126), so each call only
 compares every row's list identity and length with the last snapshot and
-copies the new tail of the rows that changed.  The device table stays
+copies the new tail of the rows that changed.  A release clears the list in
+place, so a row released and regrown between two refreshes could keep both;
+the append planner therefore marks shrunken rows (``note_released_rows``)
+before it allocates.  The device table stays
 resident: the cells that changed (one per sequence that crossed a block
 boundary, in decode) go up as (index, value) pairs together with the lengths
 (which change every step) and any per-call rows in one small pinned copy, and
@@ -119,6 +122,25 @@ def _lookup(cache, device: torch.device, stream: int) -> _Entry | None:
     if hit is not None:
         _entries.move_to_end(key)
     return hit
+
+
+def mark_shrunk_rows(ent: _Entry) -> None:
+    """Marks for a full rewrite every row whose block list is now shorter
+    than the cached copy (a release: the reference clears the list in place,
+    paged_kv.py:122-126, so once the row regrows, identity and length alone
+    cannot show that its head changed)."""
+    lists = ent.lists
+    counts = ent.counts
+    for r, s in enumerate(ent.states):
+        if len(s.block_ids) < counts[r]:
+            lists[r] = None
+
+
+def note_released_rows(cache, device: torch.device) -> None:
+    """Called by the append planner before it allocates blocks for ``cache``."""
+    ent = _lookup(cache, device, torch.cuda.current_stream(device).cuda_stream)
+    if ent is not None:
+        mark_shrunk_rows(ent)
 
 
 def block_table_and_lengths(cache, device: torch.device, extra: list[list[int]] | None = None):

@@ -30,7 +30,7 @@ import numpy as np
 import torch
 
 from . import _lib
-from ._metadata import block_table_and_lengths
+from ._metadata import block_table_and_lengths, note_released_rows
 from ._staging import stage_int32
 
 
@@ -255,6 +255,8 @@ def plan_append(cache, k_new: torch.Tensor, lengths) -> list[int]:
     n = np.clip(np.asarray(lengths, dtype=np.int64), 0, T)
     if n.any():
         pool.ensure_initialized(H, D, k_new.dtype, k_new.device)
+        if k_new.device.type == "cuda":
+            note_released_rows(cache, k_new.device)
     if not all(map(operator.is_, map(_pool_of, states), itertools.repeat(pool))):
         raise ValueError("b2pa: all states of a BatchedPagedKVCache must share its pool")
     start = np.fromiter(map(_seq_len_of, states), dtype=np.int64, count=len(states))

@@ -153,3 +153,45 @@ def test_decode_repeatable_and_stream_safe(cuda_device):
     out2, _ = _random_decode(cuda_device, B=33, H=8, D=128, bs=16, dtype=torch.bfloat16, lmin=1, lmax=2000, seed=9)
     assert torch.equal(out1, out2)
     _check(out1, ref, torch.bfloat16)
+
+
+def test_split_decode_reuses_workspace_and_replays_in_a_graph(cuda_device):
+    """Split sequences go through the combine launch: repeated calls on one
+    workspace and CUDA-graph replays of the kernel call give the oracle's
+    output every time."""
+    rng = np.random.default_rng(21)
+    gen = torch.Generator().manual_seed(21)
+    B, H, D, bs = 4, 8, 128, 16
+    lens = rng.integers(3000, 7000, size=B).tolist()
+    NB = sum(-(-L // bs) for L in lens) + 5
+    kp = torch.randn(NB, H, bs, D, generator=gen).to(torch.bfloat16).to(cuda_device)
+    vp = torch.randn(NB, H, bs, D, generator=gen).to(torch.bfloat16).to(cuda_device)
+    tables = random_tables(rng, lens, NB, bs)
+    cache = build_cache(b2pa, kp, vp, tables, lens, bs)
+    q = strided_q(B, H, 1, D, torch.bfloat16, cuda_device, gen)
+    ref = orc.paged_attention_c(q.float().cpu().numpy(), kp.float().cpu().numpy(), vp.float().cpu().numpy(), tables,
+                                lens, [1] * B)
+    from b2pa.paged_kv import device_metadata
+
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            out = b2pa.paged_attention("b200_paged", q, cache, 1)
+            _check(out, ref, torch.bfloat16)
+        # capture the kernel call alone (metadata prepared outside the graph)
+        table, seq_lens, max_pages = device_metadata(cache, torch.device(cuda_device))
+        table = table[:, :max_pages]
+        cur = torch.ones(B, dtype=torch.int32, device=cuda_device)
+        out = b2pa.paged_attention_decode_b200(q, kp, vp, table, seq_lens, cur)
+        _check(out, ref, torch.bfloat16)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            gout = b2pa.paged_attention_decode_b200(q, kp, vp, table, seq_lens, cur)
+        for _ in range(3):
+            gout.zero_()
+            g.replay()
+            s.synchronize()
+            _check(gout, ref, torch.bfloat16)
+    s.synchronize()
+    del g
+    assert b2pa.read_status(cuda_device) == 0

@@ -158,3 +158,35 @@ def test_incremental_block_table_matches_full_rebuild():
         w = full.shape[1]
         assert np.array_equal(ent.table[:, :w], full)
         assert (ent.table[:, w:] == -1).all()
+
+
+def test_release_then_regrow_between_refreshes():
+    """A release clears a row's list in place; if the row regrows before the
+    next refresh (same list object, possibly longer than before), the rows
+    marked by mark_shrunk_rows are rewritten whole, and the patch cells the
+    refresh reports rebuild the same table."""
+    from b2pa import _metadata
+
+    rng = np.random.default_rng(5)
+    pool = b2pa.LayerBlockPool(block_size=4, initial_blocks=8, growth_factor=2.0)
+    states = [b2pa.PagedKVCacheState(pool=pool) for _ in range(4)]
+    cache = b2pa.BatchedPagedKVCache(states, pool=pool)
+    cache.append_batch(_meta(4, 1, 9, 8), _meta(4, 1, 9, 8), [9, 5, 1, 7])
+    ent = _metadata._Entry(states, 256)
+    _metadata._refresh_rows(ent)
+    shadow = ent.table.copy()
+    for step in range(60):
+        for r in rng.choice(4, size=int(rng.integers(0, 3)), replace=False):
+            states[r].release()
+        _metadata.mark_shrunk_rows(ent)  # what the append planner does before allocating
+        lens = rng.integers(0, 9, size=4).tolist()
+        cache.append_batch(_meta(4, 1, 9, 8), _meta(4, 1, 9, 8), lens)
+        cells = []
+        changed, max_pages = _metadata._refresh_rows(ent, None, states, cells)
+        assert max_pages >= 0
+        flat = shadow.reshape(-1)
+        flat[np.asarray(cells[0::2], dtype=np.int64)] = cells[1::2]
+        full = cache.page_table_array()
+        w = full.shape[1]
+        assert np.array_equal(ent.table[:, :w], full)
+        assert np.array_equal(shadow, ent.table)
