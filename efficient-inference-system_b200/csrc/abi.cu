@@ -153,9 +153,27 @@ bool prefill_uses_tensor_cores(int D, int block_size, int dtype, int64_t pool_ro
 PrefillPlan make_prefill_plan(int B, int H, int T, int D, int max_pages, int block_size, int dtype) {
   PrefillPlan pl;
   const int64_t ktmax = ((int64_t)max_pages * block_size + 63) / 64;
+  pl.bm = 128;
   pl.kt_per_split = (int)(ktmax > 0 ? ktmax : 1);
   pl.nsplit_max = 1;
   pl.off_part_ml = pl.off_part_o = pl.bytes = 0;
+  if (dtype == B2PA_DTYPE_F32 && (D == 64 || D == 128)) {
+    // fp32 register-tiled kernel (64-row query tiles): a CTA takes at most
+    // kFp32KtCap key tiles, so the longest causal rows do not set the
+    // length of the whole launch; the splits are merged by the combine kernel.
+    constexpr int64_t kFp32KtCap = 8;
+    pl.bm = 64;
+    if (B <= 0 || T <= 0 || ktmax <= kFp32KtCap) return pl;
+    const int64_t ns = (ktmax + kFp32KtCap - 1) / kFp32KtCap;
+    const int64_t kt = (ktmax + ns - 1) / ns;
+    pl.kt_per_split = (int)kt;
+    pl.nsplit_max = (int)((ktmax + kt - 1) / kt);
+    const size_t slots = (size_t)B * H * T * pl.nsplit_max;
+    pl.off_part_ml = 0;
+    pl.off_part_o = align_up(8 * slots, 256);
+    pl.bytes = align_up(pl.off_part_o + 4 * slots * D, 256);
+    return pl;
+  }
   if (!prefill_uses_tensor_cores(D, block_size, dtype, 0) || B <= 0 || T <= 0 || ktmax <= 2) return pl;
   const int64_t ctas = (int64_t)B * H * ((T + 127) / 128);
   int64_t splits = 148 / ctas;

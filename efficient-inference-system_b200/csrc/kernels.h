@@ -114,6 +114,7 @@ int launch_paged_decode_f16(const AttnArgs& a, const DecodePlan& plan, cudaStrea
 // Key-range split of the tensor-core prefill (shared by the workspace query
 // and the launcher).  bytes == 0 means no split and no workspace.
 struct PrefillPlan {
+  int bm;            // query rows per CTA (128: tensor-core kernel, 64: fp32 tiled kernel)
   int kt_per_split;  // 64-key tiles per CTA
   int nsplit_max;
   size_t off_part_ml, off_part_o, bytes;

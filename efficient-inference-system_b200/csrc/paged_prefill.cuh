@@ -17,6 +17,7 @@
 #pragma once
 
 #include <algorithm>
+#include <climits>
 #include <math.h>
 
 #include "common.cuh"
@@ -46,6 +47,13 @@ struct PrefillParams {
   int B, H, T;
   float qscale;
   int32_t* status;
+  // Key-range split (fp32 tiled kernel only): CTA x = query_tile * nsplit_max
+  // + s covers key tiles [s*kt_per_split, (s+1)*kt_per_split); split rows
+  // write fp32 partials merged by prefill_combine_kernel.
+  int kt_per_split;
+  int nsplit_max;
+  float* part_o;   // [B, H, T, nsplit_max, D]
+  float* part_ml;  // [B, H, T, nsplit_max, 2]
 };
 
 template <int D>
@@ -222,6 +230,10 @@ int launch_prefill_simt(const AttnArgs& a, cudaStream_t stream) {
   p.T = a.T;
   p.qscale = a.scale * kLog2e;
   p.status = a.status;
+  p.kt_per_split = INT_MAX;  // no key split in this kernel
+  p.nsplit_max = 1;
+  p.part_o = nullptr;
+  p.part_ml = nullptr;
   const size_t smem = PrefillSmem<D>::BYTES;
   if (smem > (size_t)device_max_smem_optin())
     return set_error(B2PA_ERR_UNSUPPORTED, "paged_prefill: %zu bytes of shared memory exceed the device limit", smem);

@@ -64,6 +64,7 @@ struct PfTcParams {
   int kt_per_split;
   int nsplit_max;
   int max_cta_pages;  // capacity of the block-id array staged in shared memory
+  int bm;             // query rows per CTA of the kernel that wrote the partials
   float* part_o;   // [B, H, T, nsplit_max, D]
   float* part_ml;  // [B, H, T, nsplit_max, 2]
 };
@@ -606,6 +607,7 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
 
 // One warp per (sequence, head, query row) whose query tile was split:
 // log-sum-exp merge of the split partials, then the reference's normalisation.
+// Serves both prefill kernels (p.bm gives their query-tile height).
 template <typename T, int D, int BS>
 __global__ void __launch_bounds__(256) prefill_combine_kernel(PfTcParams p) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -616,7 +618,7 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(PfTcParams p) {
   const int b = (int)(row / ((int64_t)p.T * p.H));
   int64_t kend;
   int ntiles, nsplit;
-  prefill_tile_range(p, b, (t / 128) * 128, 128, 64, BS, &kend, &ntiles, &nsplit);
+  prefill_tile_range(p, b, (t / p.bm) * p.bm, p.bm, 64, BS, &kend, &ntiles, &nsplit);
   if (nsplit <= 1) return;
   const int64_t base = row * p.nsplit_max;
   float M = -INFINITY;
@@ -674,6 +676,7 @@ int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream) {
   const PrefillPlan plan = make_prefill_plan(a.B, a.H, a.T, a.D, a.max_pages, BS, a.dtype);
   p.kt_per_split = plan.kt_per_split;
   p.nsplit_max = plan.nsplit_max;
+  p.bm = C::BM;
   p.part_o = nullptr;
   p.part_ml = nullptr;
   if (plan.bytes > 0) {

@@ -109,6 +109,30 @@ def test_prefill_tensor_core_multi_tile(cuda_device, dtype, D):
     assert b2pa.read_status(cuda_device) == 0
 
 
+@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("bs", [8, 16, 32])
+def test_prefill_f32_tiled_multi_tile(cuda_device, D, bs):
+    # fp32 register-tiled kernel: several 64-row query tiles and 64-key tiles,
+    # a short and an empty sequence, rows padded past cur_len
+    out, ref = _random_prefill(cuda_device, B=4, H=3, D=D, bs=bs, T=200, dtype=torch.float32,
+                               prefixes=[0, 333, 1000, 0], curs=[200, 97, 200, 0], seed=D + bs)
+    _check(out, ref, torch.float32)
+    assert b2pa.read_status(cuda_device) == 0
+
+
+def test_prefill_f32_bad_block_id_is_reported(cuda_device):
+    torch.manual_seed(2)
+    kp = torch.randn(4, 2, 16, 64, device=cuda_device)
+    vp = torch.randn_like(kp)
+    cache = build_cache(b2pa, kp, vp, [[0, 9, 1]], [40], 16)  # block 9 is past the pool
+    b2pa.clear_status(cuda_device)
+    q = torch.randn(1, 2, 20, 64, device=cuda_device)
+    out = b2pa.paged_attention("b200_paged", q, cache, 20)
+    assert b2pa.read_status(cuda_device) == -3
+    b2pa.clear_status(cuda_device)
+    assert torch.isfinite(out).all()
+
+
 def test_prefill_bad_block_id_is_reported(cuda_device):
     torch.manual_seed(1)
     kp = torch.randn(4, 2, 16, 64, device=cuda_device, dtype=torch.bfloat16)
