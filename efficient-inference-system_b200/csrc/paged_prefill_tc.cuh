@@ -18,10 +18,12 @@
 //           the same tile frees its V stage.  They read block ids straight
 //           from the table, so the first loads leave before the rest of the
 //           CTA has finished setting up;
-//   MMA warp (one elected lane): S = Q.K^T (M=128, N=64, K=D) into TMEM,
-//           issued 2*NG tiles ahead, then O_g += P.V (M=128, N=D, K=64) into
-//           the TMEM accumulator of the tile's group; completion signalled
-//           with tcgen05.commit on mbarriers;
+//   two MMA issuer warps (one elected lane each): the QK warp issues
+//           S = Q.K^T (M=128, N=64, K=D) into TMEM up to 2*NG tiles ahead of
+//           the softmax; the PV warp issues O_g += P.V (M=128, N=D, K=64)
+//           into the TMEM accumulator of the tile's group.  Splitting the
+//           issue halves the serial chain of waits, MMAs and commits per tile
+//           on each issuer; hand-overs go through mbarriers (tcgen05.commit);
 //   softmax warpgroups: key tile j belongs to group j % NG; thread r of a
 //           group owns query row r: reads its S row from TMEM, masks, online
 //           softmax in the log2 domain, writes P (bf16/fp16, 128B-swizzled
@@ -111,8 +113,8 @@ struct PfTcCfg {
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
   static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
   static constexpr int OFF_BAR = OFF_P + NSLOT * P_BYTES;
-  // k_full, k_empty, v_full, v_empty [STAGES each], s_full[NSLOT], p_full[NSLOT], o_full[NG], o_final
-  static constexpr int N_BARS = 4 * STAGES + 2 * NSLOT + NG + 1;
+  // k_full, k_empty, v_full, v_empty [STAGES each], s_full, p_full, p_free [NSLOT each], o_full[NG], o_final
+  static constexpr int N_BARS = 4 * STAGES + 3 * NSLOT + NG + 1;
   static constexpr int OFF_MISC = OFF_BAR + 8 * N_BARS;  // TMEM base, abort flag
   static constexpr int OFF_ML = OFF_MISC + 16;           // per-group (m, l) of every row, for the merge
   static constexpr int OFF_BLK = OFF_ML + (NG > 1 ? 2 * NG * BM * 4 : 0);  // int32 block ids of the CTA's pages
@@ -121,10 +123,11 @@ struct PfTcCfg {
   static constexpr int TMEM_USED = NSLOT * BN + NG * D;
   static constexpr int TMEM_COLS = TMEM_USED <= 256 ? 256 : 512;
   static constexpr int SOFTMAX_THREADS = 128 * NG;
-  static constexpr int K_WARP = 4 * NG;      // K producer (also initialises the barriers)
-  static constexpr int V_WARP = 4 * NG + 1;  // V producer
-  static constexpr int MMA_WARP = 4 * NG + 2;
-  static constexpr int THREADS = SOFTMAX_THREADS + 96;
+  static constexpr int K_WARP = 4 * NG;       // K producer (also initialises the barriers)
+  static constexpr int V_WARP = 4 * NG + 1;   // V producer
+  static constexpr int QK_WARP = 4 * NG + 2;  // issues S = Q.K^T; owns the TMEM allocation
+  static constexpr int PV_WARP = 4 * NG + 3;  // issues O += P.V
+  static constexpr int THREADS = SOFTMAX_THREADS + 128;
   static_assert(D == 64 || D == 128, "tcgen05 prefill is built for head_dim 64 and 128");
   static_assert(BN % BS == 0 && 32 % PAGES == 0, "block size must divide the key tile");
   static_assert(TMEM_USED <= 512, "TMEM holds 512 columns");
@@ -138,6 +141,23 @@ __device__ __forceinline__ void named_bar_sync(int id, int n) {
 }
 __device__ __forceinline__ void named_bar_arrive(int id, int n) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// Wait by a single thread (the MMA issuer): the abort flag is read only while
+// the barrier is not yet complete.  Gives up after kWaitLimitNs, records
+// B2PA_ERR_DEVICE_TIMEOUT and raises the abort flag.
+__device__ __forceinline__ bool lane_wait(uint64_t* bar, uint32_t parity, int32_t* status, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort_flag) return false;
+    if (global_ns() - t0 > kWaitLimitNs) {
+      set_status(status, B2PA_ERR_DEVICE_TIMEOUT);
+      *abort_flag = 1;
+      return false;
+    }
+  }
 }
 
 // Waits with every lane of the warp; false (for all lanes) if any gave up.
@@ -179,8 +199,9 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
   uint64_t* v_full = bars + 2 * C::STAGES;
   uint64_t* v_empty = bars + 3 * C::STAGES;
   uint64_t* s_full = bars + 4 * C::STAGES;  // [NSLOT]
-  uint64_t* p_full = s_full + NSLOT;        // [NSLOT]
-  uint64_t* o_full = p_full + NSLOT;        // [NG]: one phase per P.V MMA of the group
+  uint64_t* p_full = s_full + NSLOT;        // [NSLOT]: P(j) written (S(j) consumed)
+  uint64_t* p_free = p_full + NSLOT;        // [NSLOT]: P.V(j) done, P buffer free
+  uint64_t* o_full = p_free + NSLOT;        // [NG]: one phase per P.V MMA of the group
   uint64_t* o_final = o_full + NG;          // one phase: every P.V of the CTA done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
@@ -202,7 +223,7 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
   int blk_pre = -1;
   {
     const int i = warp == C::K_WARP || warp == C::V_WARP ? lane : tid;
-    if (warp != C::MMA_WARP && pg0 + i < p.max_pages) blk_pre = pt_row[pg0 + i];
+    if (warp != C::QK_WARP && warp != C::PV_WARP && pg0 + i < p.max_pages) blk_pre = pt_row[pg0 + i];
   }
 
   const int64_t L = p.seq_lens[b];
@@ -230,6 +251,7 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
         for (int i = 0; i < NSLOT; ++i) {
           mbar_init(&s_full[i], 1);
           mbar_init(&p_full[i], 4);
+          mbar_init(&p_free[i], 1);
         }
         for (int g = 0; g < NG; ++g) mbar_init(&o_full[g], 1);
         mbar_init(o_final, 1);
@@ -296,17 +318,24 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
       }
       __syncwarp();
     }
-  } else if (warp == C::MMA_WARP) {
-    // ------------------------------------------------------------ MMA issue
-    tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
-    tc::tmem_relinquish();
+  } else if (warp == C::QK_WARP || warp == C::PV_WARP) {
+    // ------------------------------------------------------- MMA issuers
+    // Two issuers, one elected lane each (tcgen05.mma and commit are
+    // single-thread instructions): the QK warp issues S(j) = Q.K^T(j) into
+    // S buffer j % NSLOT once K(j) has landed and the softmax has read
+    // S(j - NSLOT); the PV warp issues O_g += P(j).V(j) for g = j % NG once
+    // P(j) and V(j) are ready, and frees P buffer j % NSLOT when done.
+    // Operations of different issuers are not ordered with each other, so
+    // every hand-over goes through an mbarrier.
+    const bool is_qk = warp == C::QK_WARP;
+    if (is_qk) {
+      tc::tmem_alloc(tmem_slot, C::TMEM_COLS);
+      tc::tmem_relinquish();
+    }
     tc::fence_before_sync();
     named_bar_sync(1, C::THREADS);
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
-    // Order: Q.K^T(0 .. NSLOT-1), then per tile j: P.V(j) once P(j) is ready,
-    // then Q.K^T(j+NSLOT) into the S buffer tile j released.  Tile j uses S/P
-    // buffer j % NSLOT and the O accumulator of group j % NG.
     constexpr int FMT = sizeof(T) == 2 && ElemTraits<T>::kDtype == B2PA_DTYPE_BF16 ? 1 : 0;
     constexpr uint32_t idesc_s = tc::idesc_f16(128, C::BN, FMT, 0, 0);
     constexpr uint32_t idesc_o = tc::idesc_f16(128, D, FMT, 0, 1);
@@ -317,12 +346,13 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
     const uint64_t dK = tc::smem_desc(smem_u32(sK), 16, 1024);
     const uint64_t dV = tc::smem_desc(smem_u32(sV), C::BN * 128, 1024);
     const uint64_t dP = tc::smem_desc(smem_u32(sP), 16, 1024);
-    auto issue_qk = [&](int j) -> bool {
-      const int st = j % C::STAGES;
-      if (!warp_wait(&k_full[st], (uint32_t)(j / C::STAGES) & 1u, p.status, abort_flag)) return false;
-      tc::fence_after_sync();
-      if (lane == 0) {
-        const uint32_t tS = tmem + (uint32_t)(j % NSLOT) * C::BN;
+    if (lane == 0 && is_qk) {
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j % C::STAGES, slot = j % NSLOT;
+        if (!lane_wait(&k_full[st], (uint32_t)(j / C::STAGES) & 1u, p.status, abort_flag)) break;
+        if (j >= NSLOT && !lane_wait(&p_full[slot], (uint32_t)(j / NSLOT - 1) & 1u, p.status, abort_flag)) break;
+        tc::fence_after_sync();
+        const uint32_t tS = tmem + (uint32_t)slot * C::BN;
         const uint64_t dKs = dK + (uint64_t)((st * C::KV_BYTES) >> 4);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
@@ -331,21 +361,19 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
           const uint64_t bd = dKs + (uint64_t)((kb * (C::BN * 128) + kk * 32) >> 4);
           tc::mma_f16_ss(tS, a, bd, idesc_s, k > 0);
         }
-        tc::commit(&s_full[j % NSLOT]);
+        tc::commit(&s_full[slot]);
         tc::commit(&k_empty[st]);
       }
-      __syncwarp();
-      return true;
-    };
-    bool ok = true;
-    for (int j = 0; j < NSLOT && j < ntiles && ok; ++j) ok = issue_qk(j);
-    for (int j = 0; j < ntiles && ok; ++j) {
-      const int st = j % C::STAGES;
-      const int slot = j % NSLOT, g = j % NG;
-      if (!warp_wait(&p_full[slot], (uint32_t)(j / NSLOT) & 1u, p.status, abort_flag)) break;
-      if (!warp_wait(&v_full[st], (uint32_t)(j / C::STAGES) & 1u, p.status, abort_flag)) break;
-      tc::fence_after_sync();
-      if (lane == 0) {
+    } else if (lane == 0) {
+      bool ok = true;
+      for (int j = 0; j < ntiles; ++j) {
+        const int st = j % C::STAGES, slot = j % NSLOT, g = j % NG;
+        if (!lane_wait(&p_full[slot], (uint32_t)(j / NSLOT) & 1u, p.status, abort_flag) ||
+            !lane_wait(&v_full[st], (uint32_t)(j / C::STAGES) & 1u, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
         const uint64_t dPs = dP + (uint64_t)((slot * C::P_BYTES) >> 4);
         const uint64_t dVs = dV + (uint64_t)((st * C::KV_BYTES) >> 4);
         const uint32_t tO = tmem + (uint32_t)(NSLOT * C::BN + g * D);
@@ -354,13 +382,12 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
           tc::mma_f16_ss(tO, dPs + (uint64_t)(k * 2), dVs + (uint64_t)(k * 128), idesc_o, j >= NG || k > 0);
         tc::commit(&o_full[g]);
         tc::commit(&v_empty[st]);
+        tc::commit(&p_free[slot]);
       }
-      __syncwarp();
-      if (j + NSLOT < ntiles) ok = issue_qk(j + NSLOT);
+      // The epilogue cannot wait on o_full by parity (it may lag by two
+      // phases); a separate single-phase barrier marks "all P.V done".
+      if (ok && ntiles > 0) tc::commit(o_final);
     }
-    // The epilogue cannot wait on o_full by parity (it may lag by two
-    // phases); a separate single-phase barrier marks "all MMAs done".
-    if (ok && ntiles > 0 && lane == 0) tc::commit(o_final);
     __syncwarp();
   } else {
     // ------------------------------------------------------------ softmax
@@ -404,10 +431,9 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
     // P values stay below 2^kRescale and the rescale of O (TMEM load, scale,
     // store) is rare.  Rescaling at the group's i-th tile j waits for the
     // group's previous P.V (tile j - NG): o_full[g] completes one phase per
-    // P.V of the group; S(j) being ready implies every MMA issued before
-    // Q.K^T(j) -- so P.V(j - 2*NG) -- is done, and P.V(j) cannot start
-    // before this warp releases P(j), so o_full[g] is in phase i-1 or i and
-    // the parity wait is exact.
+    // P.V of the group; the p_free wait before it makes P.V(j - 2*NG) done,
+    // and P.V(j) cannot start before this warp releases P(j), so o_full[g]
+    // is in phase i-1 or i and the parity wait is exact.
     constexpr float kRescale = 8.f;
     // Row maxima are taken on unscaled scores and scaled once (sc > 0); a
     // scale that is not positive is applied to the scores first instead.
@@ -474,6 +500,13 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
       // (m = -inf) holds zeros and just adopts the new max.  TMEM accesses
       // and the barrier wait are warp-collective, so the whole warp takes
       // the branch if any lane needs it (other lanes scale by 1).
+      // P buffer `slot` is free once P.V(j - NSLOT) is done.  That also makes
+      // the group's P.V two tiles back complete, which the rescale's parity
+      // wait below relies on.
+      if (j >= NSLOT && !warp_wait(&p_free[slot], (uint32_t)(j / NSLOT - 1) & 1u, p.status, abort_flag)) {
+        ok = false;
+        break;
+      }
       const bool need = mt > m + kRescale;
       const float m_new = need ? mt : m;
       const bool scale_o = need && m != -INFINITY;
@@ -505,7 +538,7 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
       float2 ls[4];  // 8 independent partial sums
 #pragma unroll
       for (int e = 0; e < 4; ++e) ls[e] = make_float2(0.f, 0.f);
-      unsigned char* sPj = sP + slot * C::P_BYTES;  // free: S(j) ready implies P.V(j - NSLOT) done
+      unsigned char* sPj = sP + slot * C::P_BYTES;
 #pragma unroll
       for (int c8 = 0; c8 < 8; ++c8) {
         float pv[8];
@@ -599,7 +632,7 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
   }
   tc::fence_before_sync();
   __syncthreads();
-  if (warp == C::MMA_WARP) {
+  if (warp == C::QK_WARP) {
     tc::fence_after_sync();
     tc::tmem_dealloc(*tmem_slot, C::TMEM_COLS);
   }
