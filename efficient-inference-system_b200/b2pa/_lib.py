@@ -105,7 +105,8 @@ def strides4(t: torch.Tensor):
 
 
 def stream_handle(device: torch.device) -> int:
-    return torch.cuda.current_stream(device).cuda_stream
+    """The raw cudaStream_t of the current stream of ``device``."""
+    return torch._C._cuda_getCurrentRawStream(device.index if device.index is not None else torch.cuda.current_device())
 
 
 # ------------------------------------------------------------ per-device state
@@ -130,7 +131,7 @@ def workspace(device: torch.device, nbytes: int) -> torch.Tensor:
     reusing the buffer across calls on that stream is safe.
     """
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    key = (idx, torch.cuda.current_stream(device).cuda_stream)
+    key = (idx, torch._C._cuda_getCurrentRawStream(idx))
     buf = _workspaces.get(key)
     if buf is None or buf.numel() < nbytes:
         size = max(int(nbytes * 1.25), 1 << 20)

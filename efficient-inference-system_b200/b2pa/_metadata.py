@@ -138,18 +138,22 @@ def mark_shrunk_rows(ent: _Entry) -> None:
 
 def note_released_rows(cache, device: torch.device) -> None:
     """Called by the append planner before it allocates blocks for ``cache``."""
-    ent = _lookup(cache, device, torch.cuda.current_stream(device).cuda_stream)
+    ent = _lookup(cache, device, _lib.stream_handle(device))
     if ent is not None:
         mark_shrunk_rows(ent)
 
 
-def block_table_and_lengths(cache, device: torch.device, extra: list[list[int]] | None = None):
+def block_table_and_lengths(cache, device: torch.device, extra: list[list[int]] | None = None,
+                            transient: bool = False):
     """Returns ``(page_table, seq_lens, *extras, max_pages)`` as int32 device
     tensors for the states of ``cache``.  ``page_table`` is ``[B, width]``
-    with ``width >= max_pages`` (pass its row stride to the kernels)."""
+    with ``width >= max_pages`` (pass its row stride to the kernels).  With
+    ``transient`` the lengths and extra rows live in a staging ring buffer:
+    valid for work enqueued on the current stream right away (the launches
+    of the calling function), not to be kept."""
     states = cache.states
     B = len(states)
-    stream = torch.cuda.current_stream(device).cuda_stream
+    stream = _lib.stream_handle(device)
     rows = 1 + (len(extra) if extra else 0)
     small = np.empty(B * rows, dtype=np.int32)
     ent = _lookup(cache, device, stream)
@@ -182,18 +186,18 @@ def block_table_and_lengths(cache, device: torch.device, extra: list[list[int]] 
         # few cells changed: send (index, value) pairs with the small rows and
         # patch the resident table in place
         packed = np.concatenate([small, np.asarray(cells, dtype=np.int32)])
-        dev = stage_int32(packed, device)
+        dev = stage_int32(packed, device, transient, stream)
         tail = dev[: B * rows]
         lib = _lib.load()
         _lib.check(lib.b2pa_patch_table(ent.dev_table.data_ptr(), ent.dev_table.numel(), dev[B * rows:].data_ptr(),
                                         n_pairs, _lib.status_buffer(device).data_ptr(), stream), "b2pa_patch_table")
     elif changed or ent.dev_table is None:
         packed = np.concatenate([ent.table.reshape(-1), small])
-        dev = stage_int32(packed, device)
+        dev = stage_int32(packed, device, False, stream)  # the resident table: kept
         ent.dev_table = dev[: B * ent.width].view(B, ent.width)
         tail = dev[B * ent.width:]
     else:
-        tail = stage_int32(small, device)
+        tail = stage_int32(small, device, transient, stream)
     outs = [ent.dev_table]
     for i in range(rows):
         outs.append(tail[B * i: B * (i + 1)])

@@ -21,7 +21,7 @@ import math
 import torch
 
 from . import _lib
-from .paged_kv import device_metadata
+from ._metadata import block_table_and_lengths
 
 # "triton_paged" is accepted so that models configured for the reference's GPU
 # backend (src/model/transformer.py:55,117) run unchanged on this one.
@@ -113,9 +113,9 @@ def paged_attention(backend: str, q: torch.Tensor, kv_cache, current_lengths) ->
         # the reference defines as a zero output (reference_paged_attention.py:67,102).
         return torch.zeros_like(q)
     if host_cur is not None:
-        page_table, seq_lens, cur, max_pages = device_metadata(kv_cache, dev, [host_cur])
+        page_table, seq_lens, cur, max_pages = block_table_and_lengths(kv_cache, dev, [host_cur], transient=True)
     else:
-        page_table, seq_lens, max_pages = device_metadata(kv_cache, dev)
+        page_table, seq_lens, max_pages = block_table_and_lengths(kv_cache, dev, transient=True)
         cur = current_lengths.to(dtype=torch.int32)
     fn = "decode" if T == 1 else "prefill"
     return _attn_call(fn, q, pool.k_blocks, pool.v_blocks, page_table, seq_lens, cur, max_pages)

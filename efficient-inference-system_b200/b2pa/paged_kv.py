@@ -239,19 +239,45 @@ def reserve_tokens(state, length: int) -> int:
 
 _seq_len_of = operator.attrgetter("seq_len")
 _pool_of = operator.attrgetter("pool")
+_SMALL_BATCH = 64  # below this, plain Python loops beat numpy's per-call overhead
 
 
 def plan_append(cache, k_new: torch.Tensor, lengths) -> list[int]:
     """Initialises the pool and allocates blocks request by request, in batch
     order (paged_kv.py:165-171); returns each request's start position.
 
-    The per-request arithmetic is vectorised; only requests whose write
-    crosses into new blocks (one in ``block_size`` per decode step) run the
-    allocation loop, still in batch order, so the LIFO free list hands out
-    the same ids as the reference's loop."""
+    For large batches the per-request arithmetic is vectorised and only
+    requests whose write crosses into new blocks (one in ``block_size`` per
+    decode step) run the allocation loop; small batches take a plain loop
+    (numpy's per-call cost dominates there).  Either way requests are served
+    in batch order, so the LIFO free list hands out the same ids as the
+    reference's loop."""
     _, H, T, D = k_new.shape
     pool = cache.pool
     states = cache.states
+    if len(states) <= _SMALL_BATCH:
+        n = [T if x > T else (0 if x < 0 else int(x)) for x in lengths]
+        if any(n):
+            pool.ensure_initialized(H, D, k_new.dtype, k_new.device)
+            if k_new.device.type == "cuda":
+                note_released_rows(cache, k_new.device)
+        bs = pool.block_size
+        allocate = pool.allocate_block
+        starts = []
+        for state, nb in zip(states, n):
+            if state.pool is not pool:
+                raise ValueError("b2pa: all states of a BatchedPagedKVCache must share its pool")
+            start = state.seq_len
+            starts.append(start)
+            if nb <= 0:
+                continue
+            # one block each time the write position reaches a block boundary
+            # (paged_kv.py:110-113): blocks for positions start .. start+nb-1
+            ids = state.block_ids
+            for _ in range((start + nb + bs - 1) // bs - (start + bs - 1) // bs):
+                ids.append(allocate())
+            state.seq_len = start + nb
+        return starts
     n = np.clip(np.asarray(lengths, dtype=np.int64), 0, T)
     if n.any():
         pool.ensure_initialized(H, D, k_new.dtype, k_new.device)
@@ -289,8 +315,12 @@ def append_batch_into(cache, k_new: torch.Tensor, v_new: torch.Tensor, current_l
     if v_new.shape != k_new.shape or v_new.dtype != k_new.dtype:
         raise ValueError("k_new and v_new must have the same shape and dtype")
     lengths = host_lengths(current_lengths, T, B)
-    clamped = np.clip(np.asarray(lengths, dtype=np.int64), 0, T)
-    any_new = bool(clamped.any())
+    if B <= _SMALL_BATCH:
+        clamped = [T if x > T else (0 if x < 0 else x) for x in lengths]
+        any_new = any(clamped)
+    else:
+        clamped = np.clip(np.asarray(lengths, dtype=np.int64), 0, T)
+        any_new = bool(clamped.any())
     if any_new and k_new.device.type not in ("cuda", "meta"):
         raise RuntimeError("b2pa: k_new must be a CUDA tensor (this package has no CPU path)")
     starts = plan_append(cache, k_new, clamped)
@@ -324,7 +354,8 @@ def _kv_append(cache, k_new: torch.Tensor, v_new: torch.Tensor, starts: list[int
         raise ValueError(f"pool on {kb.device} but k_new on {k_new.device}")
     B, H, T, D = k_new.shape
     dev = k_new.device
-    page_table, seq_lens, start_t, len_t, max_pages = device_metadata(cache, dev, [starts, lengths])
+    page_table, seq_lens, start_t, len_t, max_pages = block_table_and_lengths(cache, dev, [starts, lengths],
+                                                                               transient=True)
     lib = _lib.load()
     rc = lib.b2pa_kv_append(
         k_new.data_ptr(), _lib.strides4(k_new), v_new.data_ptr(), _lib.strides4(v_new),
@@ -339,7 +370,7 @@ def _kv_append(cache, k_new: torch.Tensor, v_new: torch.Tensor, starts: list[int
 def _zero_blocks(pool: LayerBlockPool, block_ids: list[int]) -> None:
     kb, vb = pool.k_blocks, pool.v_blocks
     dev = kb.device
-    ids = stage_int32(np.asarray(block_ids, dtype=np.int32), dev)
+    ids = stage_int32(np.asarray(block_ids, dtype=np.int32), dev, transient=True)
     lib = _lib.load()
     rc = lib.b2pa_zero_blocks(kb.data_ptr(), vb.data_ptr(), _lib.strides4(kb), kb.shape[0], ids.data_ptr(),
                               len(block_ids), kb.shape[1], kb.shape[3], kb.shape[2], _lib.dtype_code(kb.dtype),
