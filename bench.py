@@ -10,10 +10,14 @@ CausalSelfAttention.forward does per layer per decode step
 
 Arms:
   default            b2pa kernels.  ``value``: device-resident inputs, kernels
-                     launched through the C ABI, CUDA-event timed.  ``e2e``:
-                     the public API (BatchedPagedKVCache.append_batch +
-                     paged_attention) with q/k/v copied from pinned host memory
-                     and the output copied back every step.
+                     launched through the C ABI, CUDA-event timed; by default
+                     each step is one b2pa_paged_decode_append call (append
+                     fused into the decode launch; --decode-append separate
+                     times b2pa_kv_append + b2pa_paged_decode).  ``e2e``: the
+                     public API (BatchedPagedKVCache.append_batch +
+                     paged_attention, with b2pa.set_fused_append unless
+                     --decode-append separate) with q/k/v copied from pinned
+                     host memory and the output copied back every step.
   --impl reference   the CPU restatement of the reference's torch path
                      (oracle/paged_oracle.c, all host threads) on a bounded
                      sample of the same workload, rank 0 only.
@@ -57,6 +61,9 @@ def parse_args(argv=None):
     ap.add_argument("--e2e-steps", type=int, default=None, help="steps of the end-to-end leg (default: --steps)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU work of the baseline sample")
+    ap.add_argument("--decode-append", choices=["separate", "fused"], default="fused",
+                    help="separate: b2pa_kv_append then b2pa_paged_decode per step; fused: one "
+                         "b2pa_paged_decode_append (e2e: b2pa.set_fused_append)")
     ap.add_argument("--workload", choices=["decode", "prefill", "decode_f32"], default="decode",
                     help="decode: config[4] (default, the headline); prefill: config[2] chunked prefill "
                          "(bf16 and fp32); decode_f32: config[1]")
@@ -139,8 +146,11 @@ class Workload:
         return 2 * self.k_pool.numel() * 2
 
 
-def run_device_steps(torch, lib, _lib, wl: Workload, dev, first_step: int, n: int, decode_events=None):
-    """n steps of (append, decode) through the C ABI, inputs resident."""
+def run_device_steps(torch, lib, _lib, wl: Workload, dev, first_step: int, n: int, decode_events=None,
+                     fused: bool = False):
+    """n steps of (append, decode) through the C ABI, inputs resident; with
+    ``fused`` each step is one b2pa_paged_decode_append call (decode_events
+    then bracket that call)."""
     stream = torch.cuda.current_stream(dev)
     sh = stream.cuda_stream
     status = _lib.status_buffer(dev).data_ptr()
@@ -152,8 +162,22 @@ def run_device_steps(torch, lib, _lib, wl: Workload, dev, first_step: int, n: in
     s_q = _lib.strides4(wl.q)
     s_out = _lib.strides4(wl.out)
     scale = 1.0 / math.sqrt(D)
+    s_k = _lib.strides4(wl.k_new)
     for i in range(n):
         s = first_step + i
+        if fused:
+            if decode_events is not None:
+                decode_events[i][0].record(stream)
+            rc = lib.b2pa_paged_decode_append(
+                wl.q.data_ptr(), s_q, wl.k_new.data_ptr(), s_k, wl.v_new.data_ptr(), s_v, wl.k_pool.data_ptr(),
+                wl.v_pool.data_ptr(), s_pool, wl.num_blocks, wl.page_table.data_ptr(), wl.max_pages, wl.max_pages,
+                wl.seq_lens[s].data_ptr(), wl.ones.data_ptr(), wl.start_pos[s].data_ptr(), wl.ones.data_ptr(), None,
+                wl.out.data_ptr(), s_out, wl.B, H, D, BS, scale, _lib.DTYPE_BF16, ws.data_ptr(), ws.numel(),
+                status, sh)
+            _lib.check(rc, "b2pa_paged_decode_append")
+            if decode_events is not None:
+                decode_events[i][1].record(stream)
+            continue
         rc = lib.b2pa_kv_append(wl.k_new.data_ptr(), s_new, wl.v_new.data_ptr(), s_v, wl.k_pool.data_ptr(),
                                 wl.v_pool.data_ptr(), s_pool, wl.num_blocks, wl.page_table.data_ptr(),
                                 wl.max_pages, wl.max_pages, wl.start_pos[s].data_ptr(), wl.ones.data_ptr(),
@@ -170,7 +194,7 @@ def run_device_steps(torch, lib, _lib, wl: Workload, dev, first_step: int, n: in
             decode_events[i][1].record(stream)
 
 
-def count_step_launches(torch, lib, _lib, wl: Workload, dev, step: int):
+def count_step_launches(torch, lib, _lib, wl: Workload, dev, step: int, fused: bool = False):
     """Kernels one device step launches, counted from a captured (never
     replayed) CUDA graph of that step: its kernel nodes.  None if the graph
     API is unavailable."""
@@ -187,7 +211,7 @@ def count_step_launches(torch, lib, _lib, wl: Workload, dev, step: int):
         _lib.workspace(dev, lib.b2pa_paged_decode_workspace_size(wl.B, H, D, wl.max_pages, BS, _lib.DTYPE_BF16))
         torch.cuda.synchronize(dev)
         with torch.cuda.graph(g, stream=s):
-            run_device_steps(torch, lib, _lib, wl, dev, step, 1)
+            run_device_steps(torch, lib, _lib, wl, dev, step, 1, fused=fused)
     err, _, n = cudart.cudaGraphGetNodes(g.raw_cuda_graph(), 0)
     if err != cudart.cudaError_t.cudaSuccess:
         return None
@@ -366,9 +390,10 @@ def main(argv=None) -> int:
     torch.cuda.synchronize(dev)
 
     # ---------------------------------------------- device-resident (value)
-    run_device_steps(torch, lib, _lib, wl, dev, 0, args.warmup)
+    fused = args.decode_append == "fused"
+    run_device_steps(torch, lib, _lib, wl, dev, 0, args.warmup, fused=fused)
     torch.cuda.synchronize(dev)
-    launches_per_step = count_step_launches(torch, lib, _lib, wl, dev, args.warmup)
+    launches_per_step = count_step_launches(torch, lib, _lib, wl, dev, args.warmup, fused=fused)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if world > 1:
@@ -380,12 +405,12 @@ def main(argv=None) -> int:
     # under this load (the timed region alone is shorter than the sampling period).
     t_load = time.perf_counter()
     while time.perf_counter() - t_load < 0.6:
-        run_device_steps(torch, lib, _lib, wl, dev, args.warmup - 1, 1)
+        run_device_steps(torch, lib, _lib, wl, dev, args.warmup - 1, 1, fused=fused)
         torch.cuda.synchronize(dev)
     if world > 1:
         dist.barrier()
     start.record()
-    run_device_steps(torch, lib, _lib, wl, dev, args.warmup, args.steps, decode_events=ev)
+    run_device_steps(torch, lib, _lib, wl, dev, args.warmup, args.steps, decode_events=ev, fused=fused)
     end.record()
     torch.cuda.synchronize(dev)
     clock_info = clocks.stop(t_load, time.perf_counter() + 0.25)
@@ -415,6 +440,7 @@ def main(argv=None) -> int:
         host_out.copy_(out, non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
 
+    fused_before = b2pa.set_fused_append(fused)
     for _ in range(args.warmup):
         e2e_step()
     if world > 1:
@@ -426,6 +452,7 @@ def main(argv=None) -> int:
         e2e_step()
     e_end.record()
     torch.cuda.synchronize(dev)
+    b2pa.set_fused_append(fused_before)
     e2e_ms = e_start.elapsed_time(e_end)
     _lib.raise_on_device_status(dev, "e2e steps")
 
@@ -438,6 +465,8 @@ def main(argv=None) -> int:
     # roofline of the dominant kernel (decode), per launch, averaged over the timed steps
     lens_timed = [wl.lens0 + args.warmup + i + 1 for i in range(args.steps)]
     bytes_per_launch = float(np.mean([algorithmic_decode_bytes(x) for x in lens_timed]))
+    if fused:  # the fused launch also reads the new K/V rows and writes them to the pool
+        bytes_per_launch += 4 * B * H * D * 2
     peaks = _peaks()
     achieved_gbs = bytes_per_launch / (decode_avg_ms / 1e3) / 1e9
     result = {
@@ -456,6 +485,8 @@ def main(argv=None) -> int:
         "config": {
             "workload": "BASELINE config[4] large paged decode: per step one 1-token KV append + one decode "
                         "per sequence; H=32, D=128, bf16, block 16, L~U[1024,8192], pool 1.2x pages",
+            "decode_append": ("fused: one b2pa_paged_decode_append per step" if fused else
+                              "separate: b2pa_kv_append + b2pa_paged_decode per step"),
             "sequences_per_gpu": B,
             "sequences_total": total_seqs,
             "pool_gb_per_gpu": wl.pool_bytes() / 1e9,
@@ -465,7 +496,10 @@ def main(argv=None) -> int:
         "hbm_gb_per_s_decode": achieved_gbs,
         "roofline": {
             "bound": "hbm",
-            "kernel": "paged_decode (every launch of one b2pa_paged_decode call: the decode kernel and, when a sequence is split, the combine)",
+            "kernel": ("paged_decode with the fused append (every launch of one b2pa_paged_decode_append call: the "
+                       "decode kernel and, when a sequence is split, the combine)" if fused else
+                       "paged_decode (every launch of one b2pa_paged_decode call: the decode kernel and, when a "
+                       "sequence is split, the combine)"),
             "achieved": achieved_gbs,
             "peak": peaks["hbm_gbs"],
             "peak_source": peaks["source"],
@@ -482,7 +516,8 @@ def main(argv=None) -> int:
             "ms_per_step": e2e_ms / e2e_steps,
             "h2d_bytes_per_step": 3 * B * H * D * 2,
             "d2h_bytes_per_step": B * H * D * 2,
-            "path": "b2pa.BatchedPagedKVCache.append_batch + b2pa.paged_attention, pinned host inputs",
+            "path": "b2pa.BatchedPagedKVCache.append_batch + b2pa.paged_attention, pinned host inputs"
+                    + (", b2pa.set_fused_append(True)" if fused else ""),
         },
         "gpu_launches": (launches_per_step * args.steps) if launches_per_step is not None else None,
         "gpu_launches_per_step": launches_per_step,
@@ -604,6 +639,29 @@ def main_secondary(args) -> int:
         torch.cuda.synchronize()
         _lib.raise_on_device_status(dev, "secondary bench")
         step_ms = float(np.mean([a.elapsed_time(c) for a, _, c in ev]))
+        fused_ms = None
+        if T == 1:
+            # the same step as one b2pa_paged_decode_append call
+            def fused():
+                _lib.check(lib.b2pa_paged_decode_append(
+                    q.data_ptr(), _lib.strides4(q), kn.data_ptr(), _lib.strides4(kn), vn.data_ptr(),
+                    _lib.strides4(vn), kp.data_ptr(), vp.data_ptr(), _lib.strides4(kp), NB, pt.data_ptr(),
+                    max_pages, max_pages, seq.data_ptr(), cur.data_ptr(), start.data_ptr(), cur.data_ptr(), None,
+                    out.data_ptr(), _lib.strides4(out), B, Hs, Ds, bs, scale, dt, ws.data_ptr(), ws.numel(),
+                    status, sh), "decode_append")
+
+            for _ in range(max(args.warmup, 3)):
+                fused()
+            fev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(args.steps)]
+            for e0, e1 in fev:
+                flush.zero_()
+                e0.record()
+                fused()
+                e1.record()
+            torch.cuda.synchronize()
+            _lib.raise_on_device_status(dev, "secondary bench (fused)")
+            fused_ms = float(np.mean([a.elapsed_time(b) for a, b in fev]))
         attn_eager_ms = float(np.mean([b.elapsed_time(c) for _, b, c in ev]))
         # Device time without host launch gaps: the attention call captured in
         # a CUDA graph and replayed (L2 flushed before every replay).
@@ -644,7 +702,10 @@ def main_secondary(args) -> int:
                          "frac_of_hbm_peak": bytes_ / (attn_ms / 1e3) / 1e9 / peaks["hbm_gbs"]})
         else:
             bytes_ = kv_bytes + 2 * B * Hs * Ds * es + 4 * int(pages.sum()) + 8 * B
-            line.update({"tokens_per_s": B / (step_ms / 1e3), "attention_hbm_gbs": bytes_ / (attn_ms / 1e3) / 1e9,
+            line.update({"tokens_per_s": B / (step_ms / 1e3),
+                         "ms_per_step_fused_append_decode": fused_ms,
+                         "tokens_per_s_fused": B / (fused_ms / 1e3),
+                         "attention_hbm_gbs": bytes_ / (attn_ms / 1e3) / 1e9,
                          "bytes_per_launch": bytes_,
                          "frac_of_hbm_peak": bytes_ / (attn_ms / 1e3) / 1e9 / peaks["hbm_gbs"]})
         if not args.no_cpu_baseline:

@@ -15,7 +15,14 @@ from .attention import (
     paged_attention_prefill_b200,
 )
 from .integration import install_into_reference
-from .paged_kv import BatchedPagedKVCache, LayerBlockPool, PagedKVCacheState, device_metadata
+from .paged_kv import (
+    BatchedPagedKVCache,
+    LayerBlockPool,
+    PagedKVCacheState,
+    device_metadata,
+    flush_pending,
+    set_fused_append,
+)
 
 __all__ = [
     "BatchedPagedKVCache",
@@ -24,6 +31,7 @@ __all__ = [
     "SUPPORTED_BACKENDS",
     "clear_status",
     "device_metadata",
+    "flush_pending",
     "install_into_reference",
     "load_library",
     "paged_attention",
@@ -31,4 +39,5 @@ __all__ = [
     "paged_attention_prefill_b200",
     "raise_on_device_status",
     "read_status",
+    "set_fused_append",
 ]

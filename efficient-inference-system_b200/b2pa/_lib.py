@@ -28,6 +28,7 @@ STATUS_NAMES = {
     -5: "B2PA_ERR_CUDA",
     -6: "B2PA_ERR_DEVICE_TIMEOUT",
 }
+STATUS_CODES = {name: code for code, name in STATUS_NAMES.items()}
 
 # Every symbol include/b2pa.h declares, with its ctypes signature.
 _I64P = ctypes.POINTER(ctypes.c_int64)
@@ -44,6 +45,9 @@ SIGNATURES: dict[str, tuple] = {
     "b2pa_paged_decode_workspace_size": (ctypes.c_size_t, [_I, _I, _I, _I, _I, _I]),
     "b2pa_paged_decode": (_I, [_VP, _I64P, _VP, _VP, _I64P, _I64, _VP, _I64, _I, _VP, _VP, _VP, _I64P,
                                _I, _I, _I, _I, ctypes.c_float, _I, _VP, ctypes.c_size_t, _VP, _VP]),
+    "b2pa_paged_decode_append": (_I, [_VP, _I64P, _VP, _I64P, _VP, _I64P, _VP, _VP, _I64P, _I64, _VP, _I64, _I,
+                                      _VP, _VP, _VP, _VP, _VP, _VP, _I64P, _I, _I, _I, _I, ctypes.c_float, _I,
+                                      _VP, ctypes.c_size_t, _VP, _VP]),
     "b2pa_paged_decode_noalloc": (_I, [_VP, _I64P, _VP, _VP, _I64P, _I64, _VP, _I64, _I, _VP, _VP, _VP, _I64P,
                                        _I, _I, _I, _I, ctypes.c_float, _I, _VP, _VP]),
     "b2pa_paged_prefill_workspace_size": (ctypes.c_size_t, [_I, _I, _I, _I, _I, _I, _I]),

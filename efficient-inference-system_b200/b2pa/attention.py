@@ -22,6 +22,7 @@ import torch
 
 from . import _lib
 from ._metadata import block_table_and_lengths
+from .paged_kv import _kv_append, flush_pending, take_pending
 
 # "triton_paged" is accepted so that models configured for the reference's GPU
 # backend (src/model/transformer.py:55,117) run unchanged on this one.
@@ -108,6 +109,11 @@ def paged_attention(backend: str, q: torch.Tensor, kv_cache, current_lengths) ->
     elif isinstance(current_lengths, (list, tuple)):
         host_cur = [int(x) for x in current_lengths]
     pool = kv_cache.pool
+    pend = getattr(pool, "_b2pa_pending", None)
+    if pend is not None:
+        if pend.cache is kv_cache and T == 1 and pend.k_new.device == dev and pool.k_blocks.dtype == q.dtype:
+            return _decode_with_append(q, kv_cache, current_lengths, host_cur, take_pending(pool))
+        flush_pending(pool)
     if pool.k_blocks is None:
         # Nothing was ever appended to this layer: every row sees no key, which
         # the reference defines as a zero output (reference_paged_attention.py:67,102).
@@ -119,3 +125,46 @@ def paged_attention(backend: str, q: torch.Tensor, kv_cache, current_lengths) ->
         cur = current_lengths.to(dtype=torch.int32)
     fn = "decode" if T == 1 else "prefill"
     return _attn_call(fn, q, pool.k_blocks, pool.v_blocks, page_table, seq_lens, cur, max_pages)
+
+
+def _decode_with_append(q, kv_cache, current_lengths, host_cur, pend) -> torch.Tensor:
+    """Decode of ``q`` with the deferred append ``pend`` of the same batch
+    performed in the same launch (b2pa_paged_decode_append): the pair
+    append_batch + paged_attention of src/model/attention.py:56-62."""
+    pool = kv_cache.pool
+    kb, vb = pool.k_blocks, pool.v_blocks
+    dev = q.device
+    B, H, _, D = q.shape
+    if host_cur is not None:
+        page_table, seq_lens, cur, start_t, len_t, max_pages = block_table_and_lengths(
+            kv_cache, dev, [host_cur, pend.starts, pend.lengths], transient=True)
+    else:
+        page_table, seq_lens, start_t, len_t, max_pages = block_table_and_lengths(
+            kv_cache, dev, [pend.starts, pend.lengths], transient=True)
+        cur = current_lengths.to(dtype=torch.int32)
+    out = torch.empty_like(q)
+    dt = _lib.dtype_code(q.dtype)
+    lib = _lib.load()
+    block_size = kb.shape[2]
+    ws_bytes = lib.b2pa_paged_decode_workspace_size(B, H, D, max_pages, block_size, dt)
+    ws = _lib.workspace(dev, ws_bytes) if ws_bytes else None
+    k_new, v_new = pend.k_new, pend.v_new
+    rc = lib.b2pa_paged_decode_append(
+        q.data_ptr(), _lib.strides4(q), k_new.data_ptr(), _lib.strides4(k_new), v_new.data_ptr(),
+        _lib.strides4(v_new), kb.data_ptr(), vb.data_ptr(), _lib.strides4(kb), kb.shape[0],
+        page_table.data_ptr() if max_pages else None, page_table.stride(0), max_pages,
+        seq_lens.data_ptr(), cur.data_ptr(), start_t.data_ptr(), len_t.data_ptr(), pend.seq_out.data_ptr(),
+        out.data_ptr(), _lib.strides4(out), B, H, D, block_size, 1.0 / math.sqrt(D), dt,
+        ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+        _lib.status_buffer(dev).data_ptr(), _lib.stream_handle(dev))
+    if rc != 0:
+        # Nothing was launched.  Append with the ordinary kernel so the pool
+        # ends as the reference's append leaves it; a layout the fused entry
+        # does not take (rows not 4-byte aligned) then decodes separately.
+        err = _lib.last_error()
+        seq = _kv_append(kv_cache, k_new, v_new, pend.starts, pend.lengths)
+        pend.seq_out.copy_(seq)
+        if rc == _lib.STATUS_CODES["B2PA_ERR_UNSUPPORTED"]:
+            return _attn_call("decode", q, kb, vb, page_table, seq_lens, cur, max_pages)
+        raise RuntimeError(f"b2pa_paged_decode_append failed: {_lib.STATUS_NAMES.get(rc, rc)}: {err}")
+    return out

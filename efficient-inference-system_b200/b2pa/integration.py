@@ -22,20 +22,28 @@ from dataclasses import dataclass
 @dataclass
 class InstallHandle:
     originals: dict
+    fused_before: bool = False
 
     def uninstall(self) -> None:
+        from .paged_kv import set_fused_append
+
         for (module, attr), value in self.originals.items():
             setattr(module, attr, value)
+        set_fused_append(self.fused_before)
 
 
-def install_into_reference(package: str = "src") -> InstallHandle:
+def install_into_reference(package: str = "src", fuse_append: bool = False) -> InstallHandle:
     """Routes the reference's GPU attention backend through b2pa.
 
     ``package`` is the import name of the reference's source package (the
-    reference's repository root must be on ``sys.path``).
+    reference's repository root must be on ``sys.path``).  With
+    ``fuse_append`` a decode step's append_batch leaves its K/V row copy to
+    the paged_attention call that follows it, which performs it in its own
+    launch (``b2pa.set_fused_append``); the reference's forward always makes
+    that pair of calls back to back.
     """
     from .attention import paged_attention as b2pa_paged_attention
-    from .paged_kv import append_batch_into
+    from .paged_kv import append_batch_into, set_fused_append
 
     kernels_mod = importlib.import_module(f"{package}.kernels.paged_attention")
     model_attn_mod = importlib.import_module(f"{package}.model.attention")
@@ -67,4 +75,4 @@ def install_into_reference(package: str = "src") -> InstallHandle:
     model_attn_mod.paged_attention = paged_attention
     kernels_pkg.paged_attention = paged_attention
     cache_mod.BatchedPagedKVCache.append_batch = append_batch
-    return InstallHandle(originals)
+    return InstallHandle(originals, set_fused_append(fuse_append))

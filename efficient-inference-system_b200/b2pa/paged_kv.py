@@ -70,6 +70,8 @@ class LayerBlockPool:
         """Geometric growth, same arithmetic as paged_kv.py:44-73."""
         if self.num_heads is None or self.head_dim is None or self.dtype is None or self.device is None:
             raise ValueError("Pool must be initialized before growth.")
+        if getattr(self, "_b2pa_pending", None) is not None:
+            flush_pending(self)  # the copy below must carry the pending row
         grow_by = max(
             min_extra_blocks,
             self.initial_blocks if self.capacity_blocks == 0
@@ -103,6 +105,8 @@ class LayerBlockPool:
         """Zeroes ``block_ids`` in one kernel launch, then frees them in order."""
         if self.k_blocks is None or self.v_blocks is None:
             return
+        if getattr(self, "_b2pa_pending", None) is not None:
+            flush_pending(self)  # a pending row must not land in a released block
         if block_ids and self.k_blocks.device.type == "cuda":
             _zero_blocks(self, block_ids)
         self.free_block_ids.extend(block_ids)
@@ -323,11 +327,77 @@ def append_batch_into(cache, k_new: torch.Tensor, v_new: torch.Tensor, current_l
         any_new = bool(clamped.any())
     if any_new and k_new.device.type not in ("cuda", "meta"):
         raise RuntimeError("b2pa: k_new must be a CUDA tensor (this package has no CPU path)")
+    pool = cache.pool
+    if getattr(pool, "_b2pa_pending", None) is not None:
+        flush_pending(pool)  # an earlier deferred append goes first
     starts = plan_append(cache, k_new, clamped)
     if any_new and k_new.device.type == "cuda":
+        if _fused_append and T == 1 and k_new.stride(3) == 1 and v_new.stride(3) == 1:
+            seq_out = torch.empty(B, dtype=torch.long, device=k_new.device)
+            try:
+                pool._b2pa_pending = _PendingAppend(cache, k_new, v_new, starts, clamped, seq_out)
+                return seq_out
+            except AttributeError:  # a pool that refuses new attributes: append now
+                pass
         seq_lens = _kv_append(cache, k_new, v_new, starts, clamped)
         return seq_lens.to(torch.long)
     return torch.tensor([s.seq_len for s in cache.states], dtype=torch.long, device=k_new.device)
+
+
+# --------------------------------------------- deferred (fused) decode append
+# With the fused append on, a decode-step append_batch (T == 1) allocates its
+# blocks and advances seq_len on the host as usual, but leaves the K/V row
+# copy pending on the pool; the paged_attention call that follows on the
+# same batch object -- the reference's order, src/model/attention.py:56-62 --
+# performs it inside its decode launch (b2pa_paged_decode_append), one launch
+# where there were two.  Every other b2pa call that touches the pool first
+# performs a pending copy with the ordinary append kernel.
+_fused_append = False
+
+
+def set_fused_append(enabled: bool) -> bool:
+    """Turns the deferred, fused decode append on or off for the process;
+    returns the previous setting.  Off by default.
+
+    While it is on, the pool bytes of the last decode-step append_batch on a
+    pool (and the int64 lengths it returned) are written by the next b2pa
+    call on that pool: normally the paged_attention of the same batch.  Code
+    that reads pool tensors directly in between, or releases or allocates
+    blocks through objects other than this package's, must call
+    ``flush_pending(pool)`` first."""
+    global _fused_append
+    prev = _fused_append
+    _fused_append = bool(enabled)
+    return prev
+
+
+class _PendingAppend:
+    __slots__ = ("cache", "k_new", "v_new", "starts", "lengths", "seq_out")
+
+    def __init__(self, cache, k_new, v_new, starts, lengths, seq_out):
+        self.cache = cache
+        self.k_new = k_new
+        self.v_new = v_new
+        self.starts = starts
+        self.lengths = lengths
+        self.seq_out = seq_out
+
+
+def take_pending(pool):
+    """Removes and returns the pool's deferred append (None if none)."""
+    pend = getattr(pool, "_b2pa_pending", None)
+    if pend is not None:
+        pool._b2pa_pending = None
+    return pend
+
+
+def flush_pending(pool) -> None:
+    """Performs the pool's deferred decode append now, with the ordinary
+    append kernel, and fills the lengths tensor append_batch returned."""
+    pend = take_pending(pool)
+    if pend is not None:
+        seq_lens = _kv_append(pend.cache, pend.k_new, pend.v_new, pend.starts, pend.lengths)
+        pend.seq_out.copy_(seq_lens)
 
 
 # ----------------------------------------------------------------- launches

@@ -272,6 +272,11 @@ AttnArgs make_attn_args(const void* q, const int64_t* qs, const void* k_pool, co
   a.workspace = workspace;
   a.workspace_bytes = workspace_bytes;
   a.status = status;
+  a.k_new = a.v_new = nullptr;
+  a.skn[0] = a.skn[1] = a.svn[0] = a.svn[1] = 0;
+  a.app_start = a.app_len = nullptr;
+  a.app_vb = 0;
+  a.seq_out = nullptr;
   return a;
 }
 
@@ -366,6 +371,70 @@ int b2pa_paged_decode(const void* q, const int64_t q_strides[4], const void* k_p
   AttnArgs a = make_attn_args(q, q_strides, k_pool, v_pool, num_blocks, page_table, pt_stride, max_pages, seq_lens,
                               cur_lens, out, out_strides, B, H, 1, D, block_size, scale, dtype, workspace,
                               workspace_bytes, status);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  switch (dtype) {
+    case B2PA_DTYPE_F32: return launch_paged_decode_f32(a, plan, s);
+    case B2PA_DTYPE_BF16: return launch_paged_decode_bf16(a, plan, s);
+    default: return launch_paged_decode_f16(a, plan, s);
+  }
+}
+
+int b2pa_paged_decode_append(const void* q, const int64_t q_strides[4], const void* k_new,
+                             const int64_t new_k_strides[4], const void* v_new, const int64_t new_v_strides[4],
+                             void* k_pool, void* v_pool, const int64_t pool_strides[4], int64_t num_blocks,
+                             const int32_t* page_table, int64_t pt_stride, int max_pages, const int32_t* seq_lens,
+                             const int32_t* cur_lens, const int32_t* start_pos, const int32_t* lengths,
+                             int64_t* seq_lens_out, void* out, const int64_t out_strides[4], int B, int H, int D,
+                             int block_size, float scale, int dtype, void* workspace, size_t workspace_bytes,
+                             int32_t* status, void* stream) {
+  int rc = validate_attention("paged_decode_append", q, q_strides, k_pool, v_pool, pool_strides, num_blocks,
+                              page_table, pt_stride, max_pages, seq_lens, cur_lens, out, out_strides, B, H, 1, D,
+                              block_size, dtype);
+  if (rc != B2PA_OK || B == 0) return rc;
+  if (!k_new || !v_new || !new_k_strides || !new_v_strides || !start_pos || !lengths)
+    return set_error(B2PA_ERR_INVALID_ARGUMENT, "paged_decode_append: null pointer argument");
+  const int64_t* ps = pool_strides;
+  if (ps[3] != 1 || ps[2] != D || ps[1] != (int64_t)block_size * D || ps[0] != (int64_t)H * block_size * D)
+    return set_error(B2PA_ERR_UNSUPPORTED, "paged_decode_append: pools must be contiguous [num_blocks, H, block_size, D]");
+  if (new_k_strides[3] != 1 || new_v_strides[3] != 1)
+    return set_error(B2PA_ERR_UNSUPPORTED, "paged_decode_append: k_new/v_new need a unit head_dim stride");
+  // Widest access (16, 8 or 4 bytes) that every source row start allows;
+  // pool rows start at multiples of D * element size.
+  const int es = dtype_size(dtype);
+  int vb = 16;
+  auto fits = [&](int w) {
+    if ((D * es) % w || !aligned_to(k_new, w) || !aligned_to(v_new, w) || !aligned_to(k_pool, w) ||
+        !aligned_to(v_pool, w))
+      return false;
+    for (int i = 0; i < 2; ++i)
+      if ((new_k_strides[i] * es) % w || (new_v_strides[i] * es) % w) return false;
+    return true;
+  };
+  while (vb >= 4 && !fits(vb)) vb >>= 1;
+  if (vb < 4)
+    return set_error(B2PA_ERR_UNSUPPORTED, "paged_decode_append: k_new/v_new rows are not 4-byte aligned");
+  const DecodePlan plan = make_decode_plan(B, H, D, max_pages, block_size, dtype);
+  if (!workspace || workspace_bytes < plan.bytes)
+    return set_error(B2PA_ERR_WORKSPACE, "paged_decode_append: workspace of %zu bytes, %zu needed", workspace_bytes,
+                     plan.bytes);
+  if (!aligned_to(workspace, 256))
+    return set_error(B2PA_ERR_WORKSPACE, "paged_decode_append: workspace must be 256-byte aligned");
+  if (plan.max_items > INT32_MAX)
+    return set_error(B2PA_ERR_UNSUPPORTED, "paged_decode_append: %lld work items exceed the int32 plan",
+                     (long long)plan.max_items);
+  AttnArgs a = make_attn_args(q, q_strides, k_pool, v_pool, num_blocks, page_table, pt_stride, max_pages, seq_lens,
+                              cur_lens, out, out_strides, B, H, 1, D, block_size, scale, dtype, workspace,
+                              workspace_bytes, status);
+  a.k_new = k_new;
+  a.v_new = v_new;
+  a.skn[0] = new_k_strides[0];
+  a.skn[1] = new_k_strides[1];
+  a.svn[0] = new_v_strides[0];
+  a.svn[1] = new_v_strides[1];
+  a.app_start = start_pos;
+  a.app_len = lengths;
+  a.app_vb = vb;
+  a.seq_out = seq_lens_out;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   switch (dtype) {
     case B2PA_DTYPE_F32: return launch_paged_decode_f32(a, plan, s);

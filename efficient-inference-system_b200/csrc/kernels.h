@@ -90,6 +90,18 @@ struct AttnArgs {
   void* workspace;
   size_t workspace_bytes;
   int32_t* status;
+  // KV append fused into the decode launch (b2pa_paged_decode_append); unused
+  // when app_len is null.  For each b with app_len[b] > 0, row 0 of
+  // k_new/v_new ([B,H,1,D], element strides skn/svn of B and H, unit D
+  // stride) is written at position app_start[b]; app_vb is the byte width of
+  // the row copy's accesses.  seq_out (optional) receives seq_lens as int64.
+  const void* k_new;
+  const void* v_new;
+  int64_t skn[2], svn[2];
+  const int32_t* app_start;
+  const int32_t* app_len;
+  int app_vb;
+  int64_t* seq_out;
 };
 
 int launch_kv_append(const AppendArgs& a, cudaStream_t stream);

@@ -97,6 +97,14 @@ struct DecodeParams {
   float* part_ml;
   float* part_acc;
   int32_t* status;
+  // Fused KV append (null app_len: none); see decode_append_rows.
+  const void* k_new;
+  const void* v_new;
+  int64_t skn_b, skn_h, svn_b, svn_h;
+  const int32_t* app_start;
+  const int32_t* app_len;
+  int app_vb;
+  int64_t* seq_out;
 };
 
 struct StageMeta {
@@ -250,6 +258,71 @@ struct TransposeReduce {
   }
 };
 
+// Copies the new K and V rows of heads h0 .. h0+G-1 of sequence b to pool
+// row `off` of block `blk`, VB bytes per access, spread over the warp.
+template <int VB, int ROW_BYTES, int BS>
+__device__ __forceinline__ void decode_copy_new_rows(const DecodeParams& p, int b, int h0, int G, int64_t blk,
+                                                     int off, int lane, int es) {
+  using W = typename VecWord<VB>::type;
+  constexpr int CPR = ROW_BYTES / VB;  // accesses per head row
+  const char* ks = static_cast<const char*>(p.k_new);
+  const char* vs = static_cast<const char*>(p.v_new);
+  char* kp = const_cast<char*>(static_cast<const char*>(p.k_pool));
+  char* vp = const_cast<char*>(static_cast<const char*>(p.v_pool));
+  for (int i = lane; i < G * CPR; i += 32) {
+    const int hh = i / CPR;
+    const int c = i - hh * CPR;
+    const int h = h0 + hh;
+    const int64_t src_k = ((int64_t)b * p.skn_b + (int64_t)h * p.skn_h) * es + (int64_t)c * VB;
+    const int64_t src_v = ((int64_t)b * p.svn_b + (int64_t)h * p.svn_h) * es + (int64_t)c * VB;
+    const int64_t dst = ((blk * p.H + h) * BS + off) * (int64_t)ROW_BYTES + (int64_t)c * VB;
+    const W kw = *reinterpret_cast<const W*>(ks + src_k);
+    const W vw = *reinterpret_cast<const W*>(vs + src_v);
+    *reinterpret_cast<W*>(kp + dst) = kw;
+    *reinterpret_cast<W*>(vp + dst) = vw;
+  }
+}
+
+// The KV append fused into the decode launch (b2pa_paged_decode_append),
+// run by the producer warp at the start of the LAST split of (sequence b,
+// head group h0/G), before it issues any copy of that split's pages: the new
+// token sits at app_start[b] = seq_len - 1, so when it is visible it lies in
+// the last visible page, which belongs to this split; when it is not visible
+// (cur_len >= 2) nothing in the launch reads it.  No other item copies the
+// (block, head) pages of these heads.  Each lane's proxy fence orders its
+// generic-proxy stores before the bulk (async-proxy) copies that lane 0
+// issues after the warp barrier.  A row whose position is not seq_len - 1
+// (it could sit in another split's page) is skipped and reported as an
+// invalid argument; position and block checks otherwise follow
+// kv_append_kernel: out-of-range writes are skipped and reported.
+template <typename T, int D, int BS>
+__device__ __forceinline__ void decode_append_rows(const DecodeParams& p, int b, int h0, int G, int lane) {
+  if (p.app_len[b] > 0) {
+    const int64_t pos = p.app_start[b];
+    const int64_t page = pos / BS;
+    int64_t blk = -1;
+    if (pos >= 0 && page < p.max_pages) blk = p.page_table[(int64_t)b * p.pt_stride + page];
+    if (pos != (int64_t)p.seq_lens[b] - 1) {
+      if (lane == 0) set_status(p.status, B2PA_ERR_INVALID_ARGUMENT);
+    } else if (blk < 0 || blk >= p.num_blocks) {
+      if (lane == 0) set_status(p.status, B2PA_ERR_BAD_BLOCK_ID);
+    } else {
+      constexpr int ES = (int)sizeof(T);
+      constexpr int RB = D * ES;
+      const int off = (int)(pos - page * BS);
+      if (p.app_vb == 16) {
+        if constexpr (RB % 16 == 0) decode_copy_new_rows<16, RB, BS>(p, b, h0, G, blk, off, lane, ES);
+      } else if (p.app_vb == 8) {
+        if constexpr (RB % 8 == 0) decode_copy_new_rows<8, RB, BS>(p, b, h0, G, blk, off, lane, ES);
+      } else {
+        decode_copy_new_rows<4, RB, BS>(p, b, h0, G, blk, off, lane, ES);
+      }
+      fence_proxy_async_global();
+    }
+  }
+  __syncwarp();
+}
+
 template <typename T, int D, int BS>
 __global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
   using Tile = DecodeTile<T, D, BS>;
@@ -317,6 +390,7 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
       const int h0 = hg * G;
       const char* kbase = static_cast<const char*>(p.k_pool);
       const char* vbase = static_cast<const char*>(p.v_pool);
+      if (p.app_len != nullptr && s == nsplit - 1) decode_append_rows<T, D, BS>(p, b, h0, G, lane);
 
       for (int i0 = 0; i0 < count && ok; i0 += 32) {
         int blk = -1;
@@ -384,6 +458,8 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
         }
       }
     }
+    if (p.seq_out != nullptr && blockIdx.x == 0)
+      for (int b = lane; b < p.B; b += 32) p.seq_out[b] = p.seq_lens[b];
     pdl_launch_dependents();
     if (!ok && lane == 0) {
       // Gave up: let every copy this CTA started land before exiting.
@@ -605,6 +681,16 @@ int launch_decode_impl(const AttnArgs& a, const DecodePlan& plan, cudaStream_t s
   p.part_ml = reinterpret_cast<float*>(ws + plan.off_part_ml);
   p.part_acc = reinterpret_cast<float*>(ws + plan.off_part_acc);
   p.status = a.status;
+  p.k_new = a.k_new;
+  p.v_new = a.v_new;
+  p.skn_b = a.skn[0];
+  p.skn_h = a.skn[1];
+  p.svn_b = a.svn[0];
+  p.svn_h = a.svn[1];
+  p.app_start = a.app_start;
+  p.app_len = a.app_len;
+  p.app_vb = a.app_vb;
+  p.seq_out = a.seq_out;
 
   const int chunk = plan.G * Tile::HEAD_PAGE_BYTES;
   p.q_off = 2 * chunk;

@@ -136,6 +136,39 @@ B2PA_API int b2pa_paged_decode(const void* q, const int64_t q_strides[4],
                       int32_t* status, void* stream);
 
 /*
+ * Decode with the step's KV append fused into the same launch.  Replaces the
+ * pair CausalSelfAttention.forward makes for a decode step
+ * (src/model/attention.py:56-62): BatchedPagedKVCache.append_batch with
+ * T == 1 (src/cache/paged_kv.py:151-172, as b2pa_kv_append) followed by
+ * paged_attention_decode_triton (src/kernels/triton_paged_attention.py:179-217,
+ * as b2pa_paged_decode).  For each b with lengths[b] > 0, k_new[b,:,0,:] and
+ * v_new[b,:,0,:] are written to pool position start_pos[b] (block
+ * page_table[b, start_pos[b] / block_size]), and the attention of b sees
+ * them: seq_lens are the lengths after the append, as for b2pa_paged_decode,
+ * so start_pos[b] must be seq_lens[b] - 1 (rows where it is not are skipped
+ * and B2PA_ERR_INVALID_ARGUMENT is set in the status word; a block id out of
+ * range sets B2PA_ERR_BAD_BLOCK_ID).  The host allocator must already have
+ * assigned the block.  seq_lens_out
+ * (may be NULL) receives seq_lens as int64, the value append_batch returns.
+ * k_new / v_new: [B,H,1,D] element strides, unit D stride, rows 4-byte
+ * aligned.  Same workspace as b2pa_paged_decode.  Pool bytes and outputs are
+ * identical to b2pa_kv_append followed by b2pa_paged_decode.
+ */
+B2PA_API int b2pa_paged_decode_append(const void* q, const int64_t q_strides[4],
+                      const void* k_new, const int64_t new_k_strides[4],
+                      const void* v_new, const int64_t new_v_strides[4],
+                      void* k_pool, void* v_pool,
+                      const int64_t pool_strides[4], int64_t num_blocks,
+                      const int32_t* page_table, int64_t pt_stride, int max_pages,
+                      const int32_t* seq_lens, const int32_t* cur_lens,
+                      const int32_t* start_pos, const int32_t* lengths,
+                      int64_t* seq_lens_out,
+                      void* out, const int64_t out_strides[4],
+                      int B, int H, int D, int block_size, float scale, int dtype,
+                      void* workspace, size_t workspace_bytes,
+                      int32_t* status, void* stream);
+
+/*
  * Decode without a caller workspace.  No counterpart in the reference: this
  * entry point exists for callers that cannot allocate device memory (a host
  * callback or real-time thread that must not block on the allocator, a

@@ -71,7 +71,12 @@ def _run(model, prompt, n):
     return toks, logits, caches, time.perf_counter() - t0
 
 
-def test_config0_end_to_end(cuda_device):
+@pytest.mark.parametrize("fused", [False, True], ids=["append_then_decode", "fused_append"])
+def test_config0_end_to_end(cuda_device, fused):
+    """``fused``: decode-step appends deferred into the decode launch
+    (b2pa.set_fused_append)."""
+    import b2pa
+
     assert not torch.backends.cuda.matmul.allow_tf32
     g = load_golden("model_config0")
     rec = _Recorder(om.b2pa_backend())
@@ -79,10 +84,14 @@ def test_config0_end_to_end(cuda_device):
     model_r, prompt_r = om.config0_model(om.torch_reference_backend(), cuda_device)
     assert om.state_dict_digest(model_b) == bytes(g["weights_sha256"]).decode()
     assert torch.equal(prompt, prompt_r)
-    om.generate_with_cache(model_b, prompt, 2)  # warm-up (library load, workspace, first launches)
-    model_b.pools = None
-    rec.calls.clear()
-    toks_b, logits_b, caches_b, secs_b = _run(model_b, prompt, 128)
+    prev = b2pa.set_fused_append(fused)
+    try:
+        om.generate_with_cache(model_b, prompt, 2)  # warm-up (library load, workspace, first launches)
+        model_b.pools = None
+        rec.calls.clear()
+        toks_b, logits_b, caches_b, secs_b = _run(model_b, prompt, 128)
+    finally:
+        b2pa.set_fused_append(prev)
     toks_r, logits_r, caches_r, secs_r = _run(model_r, prompt, 128)
     assert torch.equal(toks_b, toks_r)
     assert np.array_equal(toks_b.numpy(), g["tokens"])
@@ -100,23 +109,25 @@ def test_config0_end_to_end(cuda_device):
     assert st_b.block_ids == g["layer0_block_ids"].tolist()
     # layer 0 inputs do not depend on attention: identical across the two backends
     assert np.array_equal(_bits(model_b.pools[0].k_blocks), _bits(model_r.pools[0].k_blocks))
-    import b2pa
-
     assert b2pa.read_status(cuda_device) == 0
     report = {"config": "BASELINE config[0]: 128-token prompt + 128 greedy tokens, batch 1, FP32",
+              "decode_append": "fused into the decode launch" if fused else "separate append kernel",
               "b2pa_seconds": secs_b, "b2pa_tokens_per_s": 128 / secs_b,
               "torch_reference_on_gpu_seconds": secs_r}
     print(json.dumps(report))
     if os.path.isdir("gpurun_out"):
-        with open("gpurun_out/e2e_config0.json", "w") as f:
+        with open(f"gpurun_out/e2e_config0{'_fused' if fused else ''}.json", "w") as f:
             json.dump(report, f)
 
 
-def test_reference_small_model_tokens(cuda_device):
+@pytest.mark.parametrize("fused", [False, True], ids=["append_then_decode", "fused_append"])
+def test_reference_small_model_tokens(cuda_device, fused):
     """The reference's own cross-backend check (tests/test_paged_attention.py:
     57-66): a 2-layer, 4-head, block-8 model, prompt (2, 16); greedy tokens of
     the GPU backend equal the torch reference path's and the reference's CPU
     run."""
+    import b2pa
+
     g = load_golden("model_tiny")
 
     def tiny(backend):
@@ -128,7 +139,11 @@ def test_reference_small_model_tokens(cuda_device):
 
     mb, pb = tiny(om.b2pa_backend())
     mr, pr = tiny(om.torch_reference_backend())
-    tb, lb, _ = om.generate_with_cache(mb, pb, 6, keep_logits=True)
+    prev = b2pa.set_fused_append(fused)
+    try:
+        tb, lb, _ = om.generate_with_cache(mb, pb, 6, keep_logits=True)
+    finally:
+        b2pa.set_fused_append(prev)
     tr, lr, _ = om.generate_with_cache(mr, pr, 6, keep_logits=True)
     assert torch.equal(tb, tr)
     assert np.array_equal(tb.numpy(), g["tokens"])

@@ -23,7 +23,20 @@ from oracle import torch_paged as tp
 pytestmark = pytest.mark.gpu
 
 
+def _warm(ex):
+    # warm-up as the reference's harness does (experiments/batching/benchmark_scheduler.py:43-61)
+    warm = osv.generate_requests(8, 1000.0, 5000, [osv.WorkloadProfile("w", 256, 256, 2, 2, 1.0)], seed=1)
+    osv.ContinuousScheduler(8, 256, 1536).run(warm, ex.prefill, ex.decode, ex.release)
+
+
+def _complete(done):
+    assert len(done) == 200
+    assert all(r.num_generated_tokens == r.max_new_tokens for r in done)
+
+
 def test_config3_serving_trace(cuda_device):
+    import b2pa
+
     base = om.b2pa_backend()
     shadow = {"n": 0, "checked": 0, "max_err": 0.0}
 
@@ -40,44 +53,49 @@ def test_config3_serving_trace(cuda_device):
     backend = om.Backend("b200_paged", base.pool_cls, base.state_cls, base.batch_cls, attention)
     model, _ = om.config0_model(backend, cuda_device)
     ex = osv.ModelExecutors(model, cuda_device)
-    # warm-up as the reference's harness does (experiments/batching/benchmark_scheduler.py:43-61)
-    warm = osv.generate_requests(8, 1000.0, 5000, [osv.WorkloadProfile("w", 256, 256, 2, 2, 1.0)], seed=1)
-    osv.ContinuousScheduler(8, 256, 1536).run(warm, ex.prefill, ex.decode, ex.release)
-    # pass 1: parity -- shadow-check one attention call in eight
-    model.pools = None
-    reqs = osv.generate_requests(200, 52.0, 5000, osv.CONFIG3_PROFILES, seed=42)
-    done, _ = osv.ContinuousScheduler(8, 256, 1536).run(reqs, ex.prefill, ex.decode, ex.release)
-    assert len(done) == 200
-    assert all(r.num_generated_tokens == r.max_new_tokens for r in done)
-    assert shadow["checked"] > 100
+    _warm(ex)
+    # pass 1: parity -- shadow-check one attention call in eight, with the
+    # decode append as a separate kernel and fused into the decode launch
+    for fused in (False, True):
+        prev = b2pa.set_fused_append(fused)
+        try:
+            model.pools = None
+            reqs = osv.generate_requests(200, 52.0, 5000, osv.CONFIG3_PROFILES, seed=42)
+            done, _ = osv.ContinuousScheduler(8, 256, 1536).run(reqs, ex.prefill, ex.decode, ex.release)
+        finally:
+            b2pa.set_fused_append(prev)
+        _complete(done)
+    assert shadow["checked"] > 200
     # pass 2: timing -- the b2pa attention alone inside the timed model calls
-    model_t, _ = om.config0_model(base, cuda_device)
-    ex = osv.ModelExecutors(model_t, cuda_device)
-    osv.ContinuousScheduler(8, 256, 1536).run(
-        osv.generate_requests(8, 1000.0, 5000, [osv.WorkloadProfile("w", 256, 256, 2, 2, 1.0)], seed=1),
-        ex.prefill, ex.decode, ex.release)
-    model_t.pools = None
-    reqs = osv.generate_requests(200, 52.0, 5000, osv.CONFIG3_PROFILES, seed=42)
-    t0 = time.perf_counter()
-    done, events = osv.ContinuousScheduler(8, 256, 1536).run(reqs, ex.prefill, ex.decode, ex.release)
-    wall = time.perf_counter() - t0
-    assert len(done) == 200
-    assert all(r.num_generated_tokens == r.max_new_tokens for r in done)
-    assert all(r.first_token_time_ms is not None for r in done)
-    import b2pa
-
-    assert b2pa.read_status(cuda_device) == 0
-    ttft = [r.first_token_latency_ms for r in done]
     report = {
         "config": "BASELINE config[3]: 200 requests @52 req/s, config[3] mix, ContinuousBatchingScheduler(8, 256, 1536), "
                   "config[0] model FP32, b2pa backend, one B200",
-        "throughput_tokens_per_s": osv.throughput_tokens_per_s(done),
-        "ttft_p50_ms": osv.percentile(ttft, 50), "ttft_p99_ms": osv.percentile(ttft, 99),
-        "latency_p99_ms": osv.percentile([r.latency_ms for r in done], 99),
-        "events": len(events), "decode_events": sum(1 for e in events if e[0] == "decode"),
-        "virtual_gpu_ms": sum(e[3] for e in events), "wall_s": wall,
         "shadow_checked_attention_calls": shadow["checked"], "shadow_max_abs_err": shadow["max_err"],
     }
+    for fused in (False, True):
+        model_t, _ = om.config0_model(base, cuda_device)
+        ex = osv.ModelExecutors(model_t, cuda_device)
+        prev = b2pa.set_fused_append(fused)
+        try:
+            _warm(ex)
+            model_t.pools = None
+            reqs = osv.generate_requests(200, 52.0, 5000, osv.CONFIG3_PROFILES, seed=42)
+            t0 = time.perf_counter()
+            done, events = osv.ContinuousScheduler(8, 256, 1536).run(reqs, ex.prefill, ex.decode, ex.release)
+            wall = time.perf_counter() - t0
+        finally:
+            b2pa.set_fused_append(prev)
+        _complete(done)
+        assert all(r.first_token_time_ms is not None for r in done)
+        assert b2pa.read_status(cuda_device) == 0
+        ttft = [r.first_token_latency_ms for r in done]
+        report["fused_append" if fused else "append_then_decode"] = {
+            "throughput_tokens_per_s": osv.throughput_tokens_per_s(done),
+            "ttft_p50_ms": osv.percentile(ttft, 50), "ttft_p99_ms": osv.percentile(ttft, 99),
+            "latency_p99_ms": osv.percentile([r.latency_ms for r in done], 99),
+            "events": len(events), "decode_events": sum(1 for e in events if e[0] == "decode"),
+            "virtual_gpu_ms": sum(e[3] for e in events), "wall_s": wall,
+        }
     print(json.dumps(report))
     if os.path.isdir("gpurun_out"):
         with open("gpurun_out/serving_config3.json", "w") as f:
