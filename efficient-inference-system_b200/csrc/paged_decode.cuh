@@ -412,6 +412,16 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
           }
           unsigned char* st = smem + (size_t)stage * p.stage_bytes;
           const int pi = i0 + j;
+          // The page copies go out first; the query and the metadata record
+          // are written while they are in flight, and the arrival that lets
+          // the consumers in comes after both (the barrier completes once the
+          // arrival and all expected bytes are in).
+          if (lane == 0 && bj >= 0) {
+            mbar_expect_tx(&full[stage], 2u * chunk_bytes);
+            const int64_t src = ((int64_t)bj * p.H + h0) * Tile::HEAD_PAGE_BYTES;
+            bulk_g2s(st, kbase + src, chunk_bytes, &full[stage]);
+            bulk_g2s(st + chunk_bytes, vbase + src, chunk_bytes, &full[stage]);
+          }
           if (pi == 0) {
             // Stage the query of this item, pre-scaled, as fp32.
             float* qs = reinterpret_cast<float*>(st + p.q_off);
@@ -439,16 +449,7 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
           }
           __threadfence_block();
           __syncwarp();
-          if (lane == 0) {
-            if (bj >= 0) {
-              mbar_arrive_expect_tx(&full[stage], 2u * chunk_bytes);
-              const int64_t src = ((int64_t)bj * p.H + h0) * Tile::HEAD_PAGE_BYTES;
-              bulk_g2s(st, kbase + src, chunk_bytes, &full[stage]);
-              bulk_g2s(st + chunk_bytes, vbase + src, chunk_bytes, &full[stage]);
-            } else {
-              mbar_arrive(&full[stage]);
-            }
-          }
+          if (lane == 0) mbar_arrive(&full[stage]);
           issued |= 1u << stage;
           issued_par = (issued_par & ~(1u << stage)) | (phase << stage);
           if (++stage == p.stages) {
