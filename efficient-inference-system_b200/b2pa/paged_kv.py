@@ -52,6 +52,7 @@ class LayerBlockPool:
         self.device: torch.device | None = None
         self.free_block_ids: list[int] = []
         self.capacity_blocks = 0
+        self._b2pa_pending = None  # a deferred decode append (set_fused_append)
 
     def ensure_initialized(self, num_heads: int, head_dim: int, dtype: torch.dtype, device: torch.device) -> None:
         """Lazily allocates the pool on first use (paged_kv.py:28-42)."""

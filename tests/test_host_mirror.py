@@ -190,3 +190,50 @@ def test_release_then_regrow_between_refreshes():
         w = full.shape[1]
         assert np.array_equal(ent.table[:, :w], full)
         assert np.array_equal(shadow, ent.table)
+
+
+def test_deferred_append_is_flushed_before_pool_changes(monkeypatch):
+    """Host ordering of the deferred (fused) decode append: a pending row copy
+    is performed before anything else touches the pool -- the next
+    append_batch, a release, pool growth -- and ``set_fused_append`` /
+    ``flush_pending`` behave as documented.  The copy itself is recorded
+    instead of launched (no GPU here)."""
+    from b2pa import paged_kv as pk
+
+    calls = []
+
+    def fake_kv_append(cache, k, v, starts, lengths):
+        calls.append((cache, list(starts), list(lengths)))
+        return torch.zeros(len(cache.states), dtype=torch.int32, device=META)
+
+    monkeypatch.setattr(pk, "_kv_append", fake_kv_append)
+    prev = b2pa.set_fused_append(True)
+    try:
+        assert b2pa.set_fused_append(True) is True
+        pool = b2pa.LayerBlockPool(16, 2, 2.0)
+        states = [b2pa.PagedKVCacheState(pool=pool) for _ in range(2)]
+        cache = b2pa.BatchedPagedKVCache(states, pool=pool)
+        # meta tensors never defer: there is nothing to launch
+        cache.append_batch(_meta(2, 1, 1, 16), _meta(2, 1, 1, 16), 1)
+        assert getattr(pool, "_b2pa_pending", None) is None
+        b2pa.flush_pending(pool)  # nothing pending: no-op
+        assert calls == []
+
+        def pend(starts):
+            out = torch.empty(2, dtype=torch.long, device=META)
+            pool._b2pa_pending = pk._PendingAppend(cache, _meta(2, 1, 1, 16), _meta(2, 1, 1, 16), starts, [1, 1],
+                                                   out)
+
+        pend([5, 6])
+        cache.append_batch(_meta(2, 1, 1, 16), _meta(2, 1, 1, 16), 1)  # flushes first
+        assert calls == [(cache, [5, 6], [1, 1])] and pool._b2pa_pending is None
+        pend([7, 8])
+        states[0].release()  # flush before the blocks are zeroed and freed
+        assert calls[-1] == (cache, [7, 8], [1, 1]) and pool._b2pa_pending is None
+        pend([9, 9])
+        pool._grow(1)  # flush before the pool tensors are replaced
+        assert calls[-1] == (cache, [9, 9], [1, 1]) and pool._b2pa_pending is None
+        assert len(calls) == 3
+    finally:
+        b2pa.set_fused_append(prev)
+    assert b2pa.set_fused_append(prev) == prev
