@@ -55,6 +55,7 @@ SIGNATURES: dict[str, tuple] = {
                                 _I, _I, _I, _I, _I, ctypes.c_float, _I, _VP, ctypes.c_size_t, _VP, _VP]),
     "b2pa_zero_blocks": (_I, [_VP, _VP, _I64P, _I64, _VP, _I, _I, _I, _I, _I, _VP, _VP]),
     "b2pa_patch_table": (_I, [_VP, _I64, _VP, _I, _VP, _VP]),
+    "b2pa_selftest_wait_timeout": (_I, [_VP, _VP, _VP]),
 }
 
 _lock = threading.Lock()

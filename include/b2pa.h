@@ -234,6 +234,17 @@ B2PA_API int b2pa_zero_blocks(void* k_pool, void* v_pool, const int64_t pool_str
 B2PA_API int b2pa_patch_table(int32_t* table, int64_t n_cells, const int32_t* pairs, int n_pairs,
                      int32_t* status, void* stream);
 
+/*
+ * Failure-path self-test; no reference counterpart (the reference has no
+ * failure detection).  Launches one warp that waits, through the bounded
+ * wait every b2pa kernel uses, on an mbarrier that nothing arrives at: after
+ * about one second the wait gives up, B2PA_ERR_DEVICE_TIMEOUT is recorded in
+ * *status, *done (device int32) is set to 2 and the kernel returns, leaving
+ * the CUDA context usable.  Lets a test check the give-up path without
+ * faulting or hanging the GPU.
+ */
+B2PA_API int b2pa_selftest_wait_timeout(int32_t* status, int32_t* done, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -83,6 +83,32 @@ def test_decode_argument_validation(lib):
     assert "workspace" in _lib.last_error() or _lib.last_error() == ""
 
 
+def _decode_append(lib, **kw):
+    args = dict(q=4096, qs=(64, 64, 64, 1), kn=8192, ks=(64, 64, 64, 1), vn=12288, vs=(64, 64, 64, 1), kp=16, vp=16,
+                ps=(16 * 64, 16 * 64, 64, 1), nb=10, pt=8, pts=4, mp=4, sl=8, cl=8, st=8, ln=8, so=0, out=8192,
+                os=(64, 64, 64, 1), B=1, H=1, D=64, bs=16, dt=0, ws=256, wsb=1 << 30)
+    args.update(kw)
+    i64 = lambda t: (ctypes.c_int64 * 4)(*t)
+    return lib.b2pa_paged_decode_append(
+        args["q"], i64(args["qs"]), args["kn"], i64(args["ks"]), args["vn"], i64(args["vs"]), args["kp"], args["vp"],
+        i64(args["ps"]), args["nb"], args["pt"], args["pts"], args["mp"], args["sl"], args["cl"], args["st"],
+        args["ln"], args["so"] or None, args["out"], i64(args["os"]), args["B"], args["H"], args["D"], args["bs"],
+        0.125, args["dt"], args["ws"], args["wsb"], None, None)
+
+
+def test_decode_append_argument_validation(lib):
+    """b2pa_paged_decode_append rejects bad arguments before launching."""
+    assert _decode_append(lib, H=0) == -1
+    assert _decode_append(lib, dt=7) == -2
+    assert _decode_append(lib, kn=0) == -1                           # null k_new
+    assert _decode_append(lib, st=0) == -1                           # null start positions
+    assert _decode_append(lib, ks=(64, 64, 64, 2)) == -2             # non-unit head_dim stride
+    assert _decode_append(lib, vn=12290) == -2                       # new V rows not 4-byte aligned
+    assert _decode_append(lib, ps=(1, 16 * 64, 64, 1)) == -2         # pools not contiguous
+    assert _decode_append(lib, wsb=16) == -4                         # workspace too small
+    assert _decode_append(lib, B=0) == 0                             # empty batch: nothing to do
+
+
 def test_workspace_size_is_monotone(lib):
     f = lib.b2pa_paged_decode_workspace_size
     a = f(64, 8, 64, 65, 16, 0)

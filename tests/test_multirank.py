@@ -57,3 +57,50 @@ def test_partition_and_max_reduction(tmp_path):
     assert len(weak[0]) == len(weak[1]) == 37           # weak: 37 per rank
     assert sorted(x for p in weak for x in p) == sorted(bench.all_lengths(74).tolist())
     assert np.load(tmp_path / "max.npy").tolist() == [2.0, 5.0]
+
+
+def _failing_worker(rank: int, world: int, port: int, out_dir: str, mode: str) -> None:
+    """Rank 1 leaves (``mode == "exit"``) or stalls past the process-group
+    timeout (``"slow"``) instead of joining the timing reduction; rank 0 must
+    get an error from that collective, not wait for ever."""
+    import datetime
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    import bench
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=3))
+    if rank == 1:
+        if mode == "slow":
+            time.sleep(8)
+        os._exit(0)  # leaves between steps, with no collective in flight
+    t0 = time.monotonic()
+    try:
+        bench.max_over_ranks([1.0], torch.device("cpu"), world)
+        outcome = "returned"
+    except Exception as e:  # the backend's error type differs between closed peers and timeouts
+        outcome = "raised " + type(e).__name__
+    with open(os.path.join(out_dir, f"rank0_{mode}.txt"), "w") as f:
+        f.write(f"{outcome} {time.monotonic() - t0:.2f}")
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["exit", "slow"])
+def test_lost_rank_ends_the_reduction_with_an_error(tmp_path, mode):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=_failing_worker, args=(r, 2, port, str(tmp_path), mode)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=60)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    assert not alive, "a rank hung"
+    outcome, secs = (tmp_path / f"rank0_{mode}.txt").read_text().rsplit(" ", 1)
+    assert outcome.startswith("raised"), outcome
+    assert float(secs) < 30
