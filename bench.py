@@ -429,15 +429,14 @@ def main(argv=None) -> int:
     lens_now = wl.lens0 + args.warmup + args.steps
     cache = build_public_cache(b2pa, wl, lens_now)
     B = wl.B
-    host_k = torch.randn(B, 1, H * D, dtype=torch.bfloat16).pin_memory()
-    host_v = torch.randn(B, 1, H * D, dtype=torch.bfloat16).pin_memory()
-    host_q = torch.randn(B, 1, H * D, dtype=torch.bfloat16).pin_memory()
+    # the step's new K, V and q as a fused QKV projection lays them out
+    # ([B, 1, 3, H, D]), in pinned host memory; one copy up per step
+    host_kvq = torch.randn(B, 1, 3, H, D, dtype=torch.bfloat16).pin_memory()
     host_out = torch.empty(B, H, 1, D, dtype=torch.bfloat16).pin_memory()
 
     def e2e_step():
-        k = host_k.to(dev, non_blocking=True).view(B, 1, H, D).transpose(1, 2)
-        v = host_v.to(dev, non_blocking=True).view(B, 1, H, D).transpose(1, 2)
-        q = host_q.to(dev, non_blocking=True).view(B, 1, H, D).transpose(1, 2)
+        kvq = host_kvq.to(dev, non_blocking=True)
+        k, v, q = (kvq[:, :, i].transpose(1, 2) for i in range(3))
         cache.append_batch(k, v, 1)
         out = b2pa.paged_attention("b200_paged", q, cache, 1)
         host_out.copy_(out, non_blocking=True)
