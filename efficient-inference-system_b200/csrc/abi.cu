@@ -149,36 +149,15 @@ bool prefill_uses_tensor_cores(int D, int block_size, int dtype, int64_t pool_ro
          (block_size == 8 || block_size == 16 || block_size == 32) && pool_rows <= ((int64_t)1 << 31);
 }
 
-// Split the key range of the tensor-core prefill when the (query tile, head,
-// sequence) CTAs alone would leave most SMs idle.  The split CTAs must fit in
-// one wave of one CTA per SM of a 148-SM part: measured on config[2], a second
-// wave or a second resident CTA per SM costs more (combine pass, shared SM)
-// than the shorter key walks save.  At least 2 key tiles per CTA.
-PrefillPlan make_prefill_plan(int B, int H, int T, int D, int max_pages, int block_size, int dtype) {
-  PrefillPlan pl;
-  const int64_t ktmax = ((int64_t)max_pages * block_size + 63) / 64;
-  pl.bm = 128;
-  pl.kt_per_split = (int)(ktmax > 0 ? ktmax : 1);
-  pl.nsplit_max = 1;
-  pl.off_part_ml = pl.off_part_o = pl.bytes = 0;
-  if (dtype == B2PA_DTYPE_F32 && (D == 64 || D == 128)) {
-    // fp32 register-tiled kernel (64-row query tiles): a CTA takes at most
-    // kFp32KtCap key tiles, so the longest causal rows do not set the
-    // length of the whole launch; the splits are merged by the combine kernel.
-    constexpr int64_t kFp32KtCap = 8;
-    pl.bm = 64;
-    if (B <= 0 || T <= 0 || ktmax <= kFp32KtCap) return pl;
-    const int64_t ns = (ktmax + kFp32KtCap - 1) / kFp32KtCap;
-    const int64_t kt = (ktmax + ns - 1) / ns;
-    pl.kt_per_split = (int)kt;
-    pl.nsplit_max = (int)((ktmax + kt - 1) / kt);
-    const size_t slots = (size_t)B * H * T * pl.nsplit_max;
-    pl.off_part_ml = 0;
-    pl.off_part_o = align_up(8 * slots, 256);
-    pl.bytes = align_up(pl.off_part_o + 4 * slots * D, 256);
-    return pl;
-  }
-  if (!prefill_uses_tensor_cores(D, block_size, dtype, 0) || B <= 0 || T <= 0 || ktmax <= 2) return pl;
+// Split the key range of the tensor-core prefill (query tiles of 128 rows)
+// when the (query tile, head, sequence) CTAs alone would leave most SMs
+// idle.  The split CTAs must fit in one wave of one CTA per SM of a 148-SM
+// part: measured on config[2], a second wave or a second resident CTA per SM
+// costs more (combine pass, shared SM) than the shorter key walks save.  At
+// least 2 key tiles per CTA.  Sets kt_per_split / nsplit_max and the
+// partials' workspace offsets; returns the partials' bytes.
+static size_t tc_key_split(PrefillPlan& pl, int B, int H, int T, int D, int64_t ktmax) {
+  if (B <= 0 || T <= 0 || ktmax <= 2) return 0;
   const int64_t ctas = (int64_t)B * H * ((T + 127) / 128);
   int64_t splits = 148 / ctas;
   // A CTA stages the block ids of its key range in shared memory: at most
@@ -187,17 +166,78 @@ PrefillPlan make_prefill_plan(int B, int H, int T, int D, int max_pages, int blo
   const int64_t min_splits = (ktmax + kt_cap - 1) / kt_cap;
   if (splits < min_splits) splits = min_splits;
   if (splits > ktmax) splits = ktmax;
-  if (splits <= 1) return pl;
+  if (splits <= 1) return 0;
   int64_t kt = (ktmax + splits - 1) / splits;
   if (kt < 2) kt = 2;
   const int64_t ns = (ktmax + kt - 1) / kt;
-  if (ns <= 1) return pl;
+  if (ns <= 1) return 0;
   pl.kt_per_split = (int)kt;
   pl.nsplit_max = (int)ns;
   const size_t slots = (size_t)B * H * T * ns;
   pl.off_part_ml = 0;
   pl.off_part_o = align_up(8 * slots, 256);
+  return align_up(pl.off_part_o + 4 * slots * D, 256);
+}
+
+static bool prefill_f32_split_tc(int D, int block_size, int64_t split_rows) {
+  return D == 64 && (block_size == 8 || block_size == 16 || block_size == 32) && split_rows > 0 &&
+         split_rows <= ((int64_t)1 << 31);
+}
+
+static PrefillPlan empty_prefill_plan(int64_t ktmax) {
+  PrefillPlan pl;
+  pl.bm = 128;
+  pl.kt_per_split = (int)(ktmax > 0 ? ktmax : 1);
+  pl.nsplit_max = 1;
+  pl.split_tc = 0;
+  pl.off_part_ml = pl.off_part_o = pl.off_split_k = pl.off_split_v = pl.off_slots = pl.off_flag = 0;
+  pl.bytes = 0;
+  return pl;
+}
+
+PrefillPlan make_prefill_plan_f32_tiled(int B, int H, int T, int D, int max_pages, int block_size) {
+  // fp32 register-tiled kernel (64-row query tiles): a CTA takes at most
+  // kFp32KtCap key tiles, so the longest causal rows do not set the length
+  // of the whole launch; the splits are merged by the combine kernel.
+  constexpr int64_t kFp32KtCap = 8;
+  const int64_t ktmax = ((int64_t)max_pages * block_size + 63) / 64;
+  PrefillPlan pl = empty_prefill_plan(ktmax);
+  pl.bm = 64;
+  if (B <= 0 || T <= 0 || ktmax <= kFp32KtCap) return pl;
+  const int64_t ns = (ktmax + kFp32KtCap - 1) / kFp32KtCap;
+  const int64_t kt = (ktmax + ns - 1) / ns;
+  pl.kt_per_split = (int)kt;
+  pl.nsplit_max = (int)((ktmax + kt - 1) / kt);
+  const size_t slots = (size_t)B * H * T * pl.nsplit_max;
+  pl.off_part_ml = 0;
+  pl.off_part_o = align_up(8 * slots, 256);
   pl.bytes = align_up(pl.off_part_o + 4 * slots * D, 256);
+  return pl;
+}
+
+PrefillPlan make_prefill_plan(int B, int H, int T, int D, int max_pages, int block_size, int dtype) {
+  const int64_t ktmax = ((int64_t)max_pages * block_size + 63) / 64;
+  PrefillPlan pl = empty_prefill_plan(ktmax);
+  if (dtype == B2PA_DTYPE_F32 && B > 0 && T > 0 &&
+      prefill_f32_split_tc(D, block_size, (int64_t)B * max_pages * H * block_size)) {
+    // fp32, head_dim 64: the tensor-core kernel on fp16 hi/lo copies of the
+    // pages (B * max_pages slots of H pages, K and V, 2 * D halves per row),
+    // after the partials of its key-range split; then the range flag.
+    pl.split_tc = 1;
+    const size_t part = tc_key_split(pl, B, H, T, D, ktmax);
+    const size_t slot_bytes = (size_t)H * block_size * 2 * D * 2;
+    const size_t nslots = (size_t)B * max_pages;
+    pl.off_split_k = align_up(part, 256);
+    pl.off_split_v = align_up(pl.off_split_k + nslots * slot_bytes, 256);
+    pl.off_slots = align_up(pl.off_split_v + nslots * slot_bytes, 256);
+    pl.off_flag = align_up(pl.off_slots + 4 * nslots, 256);
+    pl.bytes = pl.off_flag + 256;
+    return pl;
+  }
+  if (dtype == B2PA_DTYPE_F32 && (D == 64 || D == 128))
+    return make_prefill_plan_f32_tiled(B, H, T, D, max_pages, block_size);
+  if (!prefill_uses_tensor_cores(D, block_size, dtype, 0)) return pl;
+  pl.bytes = tc_key_split(pl, B, H, T, D, ktmax);
   return pl;
 }
 

@@ -129,9 +129,13 @@ struct PrefillPlan {
   int bm;            // query rows per CTA (128: tensor-core kernel, 64: fp32 tiled kernel)
   int kt_per_split;  // 64-key tiles per CTA
   int nsplit_max;
-  size_t off_part_ml, off_part_o, bytes;
+  int split_tc;      // fp32 on the tensor cores: pages split into fp16 hi/lo in the workspace
+  // split_tc: split pages, slot table and the out-of-range flag
+  size_t off_part_ml, off_part_o, off_split_k, off_split_v, off_slots, off_flag, bytes;
 };
 PrefillPlan make_prefill_plan(int B, int H, int T, int D, int max_pages, int block_size, int dtype);
+// The fp32 register-tiled kernel's plan (its workspace offsets from 0).
+PrefillPlan make_prefill_plan_f32_tiled(int B, int H, int T, int D, int max_pages, int block_size);
 bool prefill_uses_tensor_cores(int D, int block_size, int dtype, int64_t pool_rows);
 
 int launch_paged_prefill_f32(const AttnArgs& a, cudaStream_t s);

@@ -54,6 +54,10 @@ struct PrefillParams {
   int nsplit_max;
   float* part_o;   // [B, H, T, nsplit_max, D]
   float* part_ml;  // [B, H, T, nsplit_max, 2]
+  // Backup launch (general kernel only): when not null, the kernel does
+  // nothing unless *run_if == run_epoch.
+  const uint32_t* run_if;
+  uint32_t run_epoch;
 };
 
 template <int D>
@@ -72,6 +76,7 @@ struct PrefillSmem {
 template <typename T, int D, int BS>
 __global__ void __launch_bounds__(kPfThreads) paged_prefill_simt_kernel(PrefillParams p) {
   using S = PrefillSmem<D>;
+  if (p.run_if != nullptr && *p.run_if != p.run_epoch) return;  // a backup launch with nothing to redo
   extern __shared__ __align__(16) float psm[];
   float* Qs = psm;
   float* Ks = Qs + S::Q_FLOATS;
@@ -206,8 +211,11 @@ __global__ void __launch_bounds__(kPfThreads) paged_prefill_simt_kernel(PrefillP
   }
 }
 
+// run_if / run_epoch: a backup launch, which does nothing unless *run_if ==
+// run_epoch (the fp16-split tensor-core kernel met an input out of range).
 template <typename T, int D, int BS>
-int launch_prefill_simt(const AttnArgs& a, cudaStream_t stream) {
+int launch_prefill_simt(const AttnArgs& a, cudaStream_t stream, const uint32_t* run_if = nullptr,
+                        uint32_t run_epoch = 0) {
   PrefillParams p;
   p.q = a.q;
   p.sq_b = a.sq[0];
@@ -232,6 +240,8 @@ int launch_prefill_simt(const AttnArgs& a, cudaStream_t stream) {
   p.status = a.status;
   p.kt_per_split = INT_MAX;  // no key split in this kernel
   p.nsplit_max = 1;
+  p.run_if = run_if;
+  p.run_epoch = run_epoch;
   p.part_o = nullptr;
   p.part_ml = nullptr;
   const size_t smem = PrefillSmem<D>::BYTES;

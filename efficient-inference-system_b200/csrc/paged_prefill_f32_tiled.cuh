@@ -315,11 +315,13 @@ int launch_prefill_f32_tiled(const AttnArgs& a, cudaStream_t stream) {
   p.T = a.T;
   p.qscale = a.scale * kLog2e;
   p.status = a.status;
-  const PrefillPlan plan = make_prefill_plan(a.B, a.H, a.T, a.D, a.max_pages, BS, a.dtype);
+  const PrefillPlan plan = make_prefill_plan_f32_tiled(a.B, a.H, a.T, a.D, a.max_pages, BS);
   p.kt_per_split = plan.kt_per_split;
   p.nsplit_max = plan.nsplit_max;
   p.part_o = nullptr;
   p.part_ml = nullptr;
+  p.run_if = nullptr;
+  p.run_epoch = 0;
   if (plan.bytes > 0) {
     if (!a.workspace || a.workspace_bytes < plan.bytes)
       return set_error(B2PA_ERR_WORKSPACE, "paged_prefill: workspace of %zu bytes, %zu needed", a.workspace_bytes,

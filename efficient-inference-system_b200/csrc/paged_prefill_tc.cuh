@@ -39,6 +39,8 @@
 
 #include <cuda.h>
 
+#include <type_traits>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "tcgen05.cuh"
@@ -69,7 +71,18 @@ struct PfTcParams {
   int bm;             // query rows per CTA of the kernel that wrote the partials
   float* part_o;   // [B, H, T, nsplit_max, D]
   float* part_ml;  // [B, H, T, nsplit_max, 2]
+  // fp32 variant: set to `epoch` (a number of this call) when an input lies
+  // outside the range the fp16 hi/lo split represents; the kernel then stops,
+  // and the fp32 CUDA-core kernel launched after it recomputes the call.
+  // Marking with the call's number needs no reset between calls.
+  uint32_t* range_flag;
+  uint32_t epoch;
 };
+
+// Inputs of the fp32 variant must stay below 2^15 in magnitude (fp16 holds
+// up to 65504; the lo part and the fp32 accumulations then stay in range).
+// NaN and infinities fail the test too, so the CUDA-core kernel sees them.
+constexpr float kSplitRange = 32768.f;
 
 // Key tiles of query tile `t0` of sequence b, and its number of splits.
 __device__ __forceinline__ void prefill_tile_range(const PfTcParams& p, int b, int t0, int bm, int bn, int bs,
@@ -88,26 +101,42 @@ __device__ __forceinline__ void prefill_tile_range(const PfTcParams& p, int b, i
   *nsplit_out = ns < 1 ? 1 : ns;
 }
 
-template <int D, int BS>
+// SPLIT: the fp32 variant.  Every fp32 operand x (q, the K/V pages, P) is
+// carried as two fp16 tiles, hi = fp16(x) and lo = fp16(x - hi), which
+// together hold 22 significant bits, and each product is taken as
+// hi*hi + hi*lo + lo*hi on the fp16 tensor cores with fp32 accumulation (the
+// dropped lo*lo and the residual are ~2^-21 of the product).  A bf16 split
+// (16 bits) was built first and missed the fp32 tolerance (atol 1e-5) on a
+// few elements; fp16 meets it, but only holds |x| < 65504, so inputs at or
+// above 2^15 (or not finite) raise range_flag and the call is recomputed by
+// the general fp32 CUDA-core kernel, launched after this one as a backup that
+// does nothing otherwise.  The K/V pages are split into a workspace copy
+// beforehand (prefill_split_pages_kernel); q and P are split in the kernel.
+template <int D, int BS, bool SPLIT = false>
 struct PfTcCfg {
   static constexpr int BM = 128;         // query rows per CTA (UMMA M)
   static constexpr int BN = 64;          // keys per tile
   static constexpr int KB = D / 64;      // 128-byte column blocks of a row
   static constexpr int PAGES = BN / BS;  // pages per key tile
+  static constexpr int NOP = SPLIT ? 2 : 1;  // bf16 tiles per operand tile (hi, lo)
   // Softmax warpgroups.  With two, key tiles alternate between them (tile j
   // -> group j % NG) and each keeps its own running max, denominator and O
   // accumulator; the groups are merged in the epilogue.  Two groups put two
   // softmax warps on every SM sub-partition, so one warp's exponentials
   // overlap the other's TMEM loads, barrier waits and P stores.
-  static constexpr int NG = D == 64 ? 2 : 1;
+  // (The fp32 variant, with twice the operand bytes, keeps one group.)
+  static constexpr int NG = !SPLIT && D == 64 ? 2 : 1;
   static constexpr int NSLOT = 2 * NG;  // S/P buffers: two per group
   // Depth of the K ring and of the V ring.  A K stage is refilled once the
   // Q.K^T that read it is done, a V stage once its P.V is done, so each ring
   // loads up to STAGES tiles ahead of its consumer.
-  static constexpr int STAGES = D == 64 ? 6 : 4;
-  static constexpr int Q_BYTES = BM * D * 2;
-  static constexpr int KV_BYTES = BN * D * 2;
-  static constexpr int P_BYTES = BM * BN * 2;
+  static constexpr int STAGES = SPLIT ? 3 : (D == 64 ? 6 : 4);
+  static constexpr int Q_TILE = BM * D * 2;   // one bf16 / fp16 tile
+  static constexpr int KV_TILE = BN * D * 2;
+  static constexpr int P_TILE = BM * BN * 2;
+  static constexpr int Q_BYTES = NOP * Q_TILE;  // hi tile, then lo tile
+  static constexpr int KV_BYTES = NOP * KV_TILE;
+  static constexpr int P_BYTES = NOP * P_TILE;
   static constexpr int OFF_Q = 0;
   static constexpr int OFF_K = OFF_Q + Q_BYTES;
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
@@ -129,6 +158,7 @@ struct PfTcCfg {
   static constexpr int PV_WARP = 4 * NG + 3;  // issues O += P.V
   static constexpr int THREADS = SOFTMAX_THREADS + 128;
   static_assert(D == 64 || D == 128, "tcgen05 prefill is built for head_dim 64 and 128");
+  static_assert(!SPLIT || D == 64, "the fp32 variant fits shared memory for head_dim 64 only");
   static_assert(BN % BS == 0 && 32 % PAGES == 0, "block size must divide the key tile");
   static_assert(TMEM_USED <= 512, "TMEM holds 512 columns");
   static_assert(SMEM_FIXED <= 200 * 1024, "shared-memory plan");
@@ -180,11 +210,32 @@ __device__ __forceinline__ int prefill_checked_block(const PfTcParams& p, int ra
   return raw;
 }
 
+// fp32 pools take the split (hi/lo bf16) variant of the kernel.
+template <typename T>
+constexpr bool kPfSplit = std::is_same<T, float>::value;
+
+// Eight fp32 values as two 16-byte words of fp16: hi = round(x), lo =
+// round(x - hi) (element 0 in the lowest bytes, as the tiles store them).
+__device__ __forceinline__ void split_f16x8(const float (&f)[8], uint4& hi, uint4& lo) {
+  uint32_t h[4], l[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __half2 hh = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    const float2 hf = __half22float2(hh);
+    const __half2 ll = __floats2half2_rn(f[2 * i] - hf.x, f[2 * i + 1] - hf.y);
+    h[i] = *reinterpret_cast<const uint32_t*>(&hh);
+    l[i] = *reinterpret_cast<const uint32_t*>(&ll);
+  }
+  hi = make_uint4(h[0], h[1], h[2], h[3]);
+  lo = make_uint4(l[0], l[1], l[2], l[3]);
+}
+
 template <typename T, int D, int BS>
-__global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
+__global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             PfTcParams p) {
-  using C = PfTcCfg<D, BS>;
+  constexpr bool SPLIT = kPfSplit<T>;
+  using C = PfTcCfg<D, BS, SPLIT>;
   constexpr int NG = C::NG, NSLOT = C::NSLOT;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
@@ -209,6 +260,15 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
   int* sblk = reinterpret_cast<int*>(smem + C::OFF_BLK);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if constexpr (SPLIT) {
+    // an input out of the split's range was seen (pre-pass or another CTA):
+    // the CUDA-core kernel that follows recomputes the call.  One read,
+    // shared, so the whole CTA takes the same branch.
+    __shared__ int stop;
+    if (tid == 0) stop = *reinterpret_cast<volatile uint32_t*>(p.range_flag) == p.epoch;
+    __syncthreads();
+    if (stop) return;
+  }
   const int split = blockIdx.x % p.nsplit_max;
   const int t0 = (blockIdx.x / p.nsplit_max) * C::BM;
   const int h = blockIdx.y;
@@ -290,15 +350,17 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
         const int blk = __shfl_sync(kFullMask, blk_lane, (lp + pg) & 31);
         blks[pg] = blk;
         if (blk >= 0) {
-          bytes += (uint32_t)(BS * D * 2);
+          bytes += (uint32_t)(C::NOP * BS * D * 2);
         } else {
           // Pages that are not loaded must not hold stale or uninitialised
           // bytes: their softmax weight is 0, but 0 * NaN is NaN in P.V.
 #pragma unroll
-          for (int kb = 0; kb < C::KB; ++kb) {
-            const int off = st * C::KV_BYTES + kb * (C::BN * 128) + pg * (BS * 128);
-            for (int i = lane; i < BS * 8; i += 32) reinterpret_cast<uint4*>(ring + off)[i] = make_uint4(0, 0, 0, 0);
-          }
+          for (int op = 0; op < C::NOP; ++op)
+#pragma unroll
+            for (int kb = 0; kb < C::KB; ++kb) {
+              const int off = st * C::KV_BYTES + op * C::KV_TILE + kb * (C::BN * 128) + pg * (BS * 128);
+              for (int i = lane; i < BS * 8; i += 32) reinterpret_cast<uint4*>(ring + off)[i] = make_uint4(0, 0, 0, 0);
+            }
         }
       }
       tc::fence_proxy_async_smem();
@@ -309,11 +371,15 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
         for (int pg = 0; pg < C::PAGES; ++pg) {
           if (blks[pg] < 0) continue;
           const int row = (blks[pg] * p.H + h) * BS;
+          // split variant: the workspace rows hold hi in columns [0, D) and
+          // lo in [D, 2D)
 #pragma unroll
-          for (int kb = 0; kb < C::KB; ++kb) {
-            const int off = st * C::KV_BYTES + kb * (C::BN * 128) + pg * (BS * 128);
-            tc::tma_load_2d(ring + off, tmap, kb * 64, row, &full[st]);
-          }
+          for (int op = 0; op < C::NOP; ++op)
+#pragma unroll
+            for (int kb = 0; kb < C::KB; ++kb) {
+              const int off = st * C::KV_BYTES + op * C::KV_TILE + kb * (C::BN * 128) + pg * (BS * 128);
+              tc::tma_load_2d(ring + off, tmap, op * D + kb * 64, row, &full[st]);
+            }
         }
       }
       __syncwarp();
@@ -336,7 +402,7 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
     named_bar_sync(1, C::THREADS);
     tc::fence_after_sync();
     const uint32_t tmem = *tmem_slot;
-    constexpr int FMT = sizeof(T) == 2 && ElemTraits<T>::kDtype == B2PA_DTYPE_BF16 ? 1 : 0;
+    constexpr int FMT = !SPLIT && ElemTraits<T>::kDtype == B2PA_DTYPE_BF16 ? 1 : 0;
     constexpr uint32_t idesc_s = tc::idesc_f16(128, C::BN, FMT, 0, 0);
     constexpr uint32_t idesc_o = tc::idesc_f16(128, D, FMT, 0, 1);
     // Descriptors of the operand bases; an operand at byte offset `off` from
@@ -360,6 +426,10 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
           const uint64_t a = dQ + (uint64_t)((kb * (C::BM * 128) + kk * 32) >> 4);
           const uint64_t bd = dKs + (uint64_t)((kb * (C::BN * 128) + kk * 32) >> 4);
           tc::mma_f16_ss(tS, a, bd, idesc_s, k > 0);
+          if constexpr (SPLIT) {
+            tc::mma_f16_ss(tS, a, bd + (uint64_t)(C::KV_TILE >> 4), idesc_s, true);  // q_hi . k_lo
+            tc::mma_f16_ss(tS, a + (uint64_t)(C::Q_TILE >> 4), bd, idesc_s, true);   // q_lo . k_hi
+          }
         }
         tc::commit(&s_full[slot]);
         tc::commit(&k_empty[st]);
@@ -378,8 +448,15 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
         const uint64_t dVs = dV + (uint64_t)((st * C::KV_BYTES) >> 4);
         const uint32_t tO = tmem + (uint32_t)(NSLOT * C::BN + g * D);
 #pragma unroll
-        for (int k = 0; k < C::BN / 16; ++k)
+        for (int k = 0; k < C::BN / 16; ++k) {
           tc::mma_f16_ss(tO, dPs + (uint64_t)(k * 2), dVs + (uint64_t)(k * 128), idesc_o, j >= NG || k > 0);
+          if constexpr (SPLIT) {
+            tc::mma_f16_ss(tO, dPs + (uint64_t)(k * 2), dVs + (uint64_t)((C::KV_TILE >> 4) + k * 128), idesc_o,
+                           true);  // p_hi . v_lo
+            tc::mma_f16_ss(tO, dPs + (uint64_t)((C::P_TILE >> 4) + k * 2), dVs + (uint64_t)(k * 128), idesc_o,
+                           true);  // p_lo . v_hi
+          }
+        }
         tc::commit(&o_full[g]);
         tc::commit(&v_empty[st]);
         tc::commit(&p_free[slot]);
@@ -401,11 +478,33 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
       const int c = tid + it * C::SOFTMAX_THREADS;
       const int qr = c / (D / 8), qc = c % (D / 8);
       const int qt = t0 + qr;
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (qt < p.T)
-        v = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + (int64_t)b * p.sq_b + (int64_t)h * p.sq_h +
-                                            (int64_t)qt * p.sq_t + qc * 8);
-      *reinterpret_cast<uint4*>(sQ + (qc >> 3) * (C::BM * 128) + tc::sw128_offset(qr, qc & 7)) = v;
+      const int off = (qc >> 3) * (C::BM * 128) + tc::sw128_offset(qr, qc & 7);
+      if constexpr (SPLIT) {
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = 0.f;
+        if (qt < p.T) {
+          const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.q) + (int64_t)b * p.sq_b +
+                                                              (int64_t)h * p.sq_h + (int64_t)qt * p.sq_t + qc * 8);
+          const float4 x0 = src[0], x1 = src[1];
+          f[0] = x0.x; f[1] = x0.y; f[2] = x0.z; f[3] = x0.w;
+          f[4] = x1.x; f[5] = x1.y; f[6] = x1.z; f[7] = x1.w;
+          bool in_range = true;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) in_range = in_range && fabsf(f[e]) < kSplitRange;
+          if (!in_range) *p.range_flag = p.epoch;
+        }
+        uint4 hi, lo;
+        split_f16x8(f, hi, lo);
+        *reinterpret_cast<uint4*>(sQ + off) = hi;
+        *reinterpret_cast<uint4*>(sQ + C::Q_TILE + off) = lo;
+      } else {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (qt < p.T)
+          v = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + (int64_t)b * p.sq_b +
+                                              (int64_t)h * p.sq_h + (int64_t)qt * p.sq_t + qc * 8);
+        *reinterpret_cast<uint4*>(sQ + off) = v;
+      }
     }
     tc::fence_proxy_async_smem();
     tc::fence_before_sync();
@@ -549,9 +648,16 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
           pv[2 * e + 1] = fast_exp2(x.y);
           ls[e] = add2(ls[e], make_float2(pv[2 * e], pv[2 * e + 1]));
         }
-        Vec<T, 8> w;
-        w.from_float(pv);
-        *reinterpret_cast<uint4*>(sPj + tc::sw128_offset(r, c8)) = w.w;
+        if constexpr (SPLIT) {
+          uint4 hi, lo;
+          split_f16x8(pv, hi, lo);
+          *reinterpret_cast<uint4*>(sPj + tc::sw128_offset(r, c8)) = hi;
+          *reinterpret_cast<uint4*>(sPj + C::P_TILE + tc::sw128_offset(r, c8)) = lo;
+        } else {
+          Vec<T, 8> w;
+          w.from_float(pv);
+          *reinterpret_cast<uint4*>(sPj + tc::sw128_offset(r, c8)) = w.w;
+        }
       }
       const float2 l01 = add2(ls[0], ls[1]), l23 = add2(ls[2], ls[3]);
       l += (l01.x + l01.y) + (l23.x + l23.y);
@@ -624,9 +730,15 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS>::THREADS, 1)
         float f[8];
 #pragma unroll
         for (int e = 0; e < 8; ++e) f[e] = o[c8 * 8 + e] * inv;
-        Vec<T, 8> w;
-        w.from_float(f);
-        *reinterpret_cast<uint4*>(orow + c8 * 8) = w.w;
+        if constexpr (SPLIT) {
+          float4* o4 = reinterpret_cast<float4*>(orow + c8 * 8);
+          o4[0] = make_float4(f[0], f[1], f[2], f[3]);
+          o4[1] = make_float4(f[4], f[5], f[6], f[7]);
+        } else {
+          Vec<T, 8> w;
+          w.from_float(f);
+          *reinterpret_cast<uint4*>(orow + c8 * 8) = w.w;
+        }
       }
     }
   }
@@ -675,24 +787,129 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(PfTcParams p) {
   for (int i = 0; i < PER; ++i) orow[lane + 32 * i] = from_f32<T>(o[i] / den);
 }
 
+// The fp32 variant's first step: copies every page that the prefill of
+// sequence b reads (pages holding keys below min(seq_len, table width)) of K
+// and of V into the workspace as bf16 hi/lo rows -- row (slot * H + h) * BS
+// + r holds hi in columns [0, D) and lo in [D, 2D), slot = b * max_pages +
+// page -- and writes the slot table the kernel walks in place of the block
+// table: -1 for a page it must not read (past the sequence, a negative
+// entry, or a block id outside the pool, which is also reported).
+struct PfSplitArgs {
+  const float* k_pool;
+  const float* v_pool;
+  const int32_t* page_table;
+  int64_t pt_stride;
+  int max_pages;
+  const int32_t* seq_lens;
+  int64_t num_blocks;
+  int H;
+  __half* k_split;
+  __half* v_split;
+  int32_t* slots;
+  uint32_t* range_flag;
+  uint32_t epoch;
+  int32_t* status;
+};
+
+template <int D, int BS>
+__global__ void __launch_bounds__(128) prefill_split_pages_kernel(PfSplitArgs a) {
+  const int i = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  int64_t kend = a.seq_lens[b];
+  const int64_t cap = (int64_t)a.max_pages * BS;
+  kend = kend < cap ? kend : cap;
+  const int64_t slot = (int64_t)b * a.max_pages + i;
+  int64_t blk = -1;
+  if ((int64_t)i * BS < kend) {
+    const int32_t raw = a.page_table[(int64_t)b * a.pt_stride + i];
+    if (raw >= 0 && raw < a.num_blocks) {
+      blk = raw;
+    } else if (raw >= a.num_blocks && h == 0 && threadIdx.x == 0) {
+      set_status(a.status, B2PA_ERR_BAD_BLOCK_ID);
+    }
+  }
+  if (h == 0 && threadIdx.x == 0) a.slots[slot] = (int32_t)(blk >= 0 ? slot : -1);
+  if (blk < 0) return;
+  const int64_t src = ((blk * a.H + h) * BS) * D;
+  const int64_t dst = ((slot * a.H + h) * BS) * (2 * D);
+  bool in_range = true;
+  for (int idx = threadIdx.x; idx < BS * D / 8; idx += blockDim.x) {
+    const int r = idx / (D / 8), c8 = idx - (idx / (D / 8)) * (D / 8);
+#pragma unroll
+    for (int kv = 0; kv < 2; ++kv) {
+      const float4* s4 = reinterpret_cast<const float4*>((kv ? a.v_pool : a.k_pool) + src + (int64_t)r * D + c8 * 8);
+      const float4 x0 = s4[0], x1 = s4[1];
+      const float f[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) in_range = in_range && fabsf(f[e]) < kSplitRange;
+      uint4 hi, lo;
+      split_f16x8(f, hi, lo);
+      __half* d = (kv ? a.v_split : a.k_split) + dst + (int64_t)r * (2 * D) + c8 * 8;
+      *reinterpret_cast<uint4*>(d) = hi;
+      *reinterpret_cast<uint4*>(d + D) = lo;
+    }
+  }
+  if (!in_range) *a.range_flag = a.epoch;
+}
+
 // ----------------------------------------------------------------- host ---
 bool encode_pool_tensor_map(CUtensorMap* map, const void* pool, int64_t rows, int D, int block_size, int dtype);
 
+// epoch: the fp32 variant's number of this call (marks the range flag).
 template <typename T, int D, int BS>
-int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream) {
-  using C = PfTcCfg<D, BS>;
+int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream, uint32_t epoch = 0) {
+  constexpr bool SPLIT = kPfSplit<T>;
+  using C = PfTcCfg<D, BS, SPLIT>;
+  const PrefillPlan plan = make_prefill_plan(a.B, a.H, a.T, a.D, a.max_pages, BS, a.dtype);
+  if (plan.bytes > 0 && (!a.workspace || a.workspace_bytes < plan.bytes))
+    return set_error(B2PA_ERR_WORKSPACE, "paged_prefill: workspace of %zu bytes, %zu needed", a.workspace_bytes,
+                     plan.bytes);
   CUtensorMap tmk, tmv;
-  const int64_t rows = a.num_blocks * a.H * BS;
-  if (!encode_pool_tensor_map(&tmk, a.k_pool, rows, D, BS, a.dtype) ||
-      !encode_pool_tensor_map(&tmv, a.v_pool, rows, D, BS, a.dtype))
-    return set_error(B2PA_ERR_CUDA, "paged_prefill: cuTensorMapEncodeTiled failed for the pools");
+  uint32_t* range_flag = nullptr;
+  const int32_t* table = a.page_table;
+  int64_t pt_stride = a.pt_stride;
+  int64_t num_blocks = a.num_blocks;
+  if constexpr (SPLIT) {
+    if (!plan.split_tc) return set_error(B2PA_ERR_UNSUPPORTED, "paged_prefill: fp32 split plan not applicable");
+    char* ws = static_cast<char*>(a.workspace);
+    PfSplitArgs sa;
+    sa.k_pool = static_cast<const float*>(a.k_pool);
+    sa.v_pool = static_cast<const float*>(a.v_pool);
+    sa.page_table = a.page_table;
+    sa.pt_stride = a.pt_stride;
+    sa.max_pages = a.max_pages;
+    sa.seq_lens = a.seq_lens;
+    sa.num_blocks = a.num_blocks;
+    sa.H = a.H;
+    sa.k_split = reinterpret_cast<__half*>(ws + plan.off_split_k);
+    sa.v_split = reinterpret_cast<__half*>(ws + plan.off_split_v);
+    sa.slots = reinterpret_cast<int32_t*>(ws + plan.off_slots);
+    sa.range_flag = reinterpret_cast<uint32_t*>(ws + plan.off_flag);
+    sa.epoch = epoch;
+    sa.status = a.status;
+    range_flag = sa.range_flag;
+    const int64_t nslots = (int64_t)a.B * a.max_pages;
+    const int64_t rows = nslots * a.H * BS;
+    if (!encode_pool_tensor_map(&tmk, sa.k_split, rows, 2 * D, BS, B2PA_DTYPE_F16) ||
+        !encode_pool_tensor_map(&tmv, sa.v_split, rows, 2 * D, BS, B2PA_DTYPE_F16))
+      return set_error(B2PA_ERR_CUDA, "paged_prefill: cuTensorMapEncodeTiled failed for the split pages");
+    prefill_split_pages_kernel<D, BS><<<dim3((unsigned)a.max_pages, (unsigned)a.H, (unsigned)a.B), 128, 0, stream>>>(
+        sa);
+    table = sa.slots;
+    pt_stride = a.max_pages;
+    num_blocks = nslots;
+  } else {
+    const int64_t rows = a.num_blocks * a.H * BS;
+    if (!encode_pool_tensor_map(&tmk, a.k_pool, rows, D, BS, a.dtype) ||
+        !encode_pool_tensor_map(&tmv, a.v_pool, rows, D, BS, a.dtype))
+      return set_error(B2PA_ERR_CUDA, "paged_prefill: cuTensorMapEncodeTiled failed for the pools");
+  }
   PfTcParams p;
   p.q = a.q;
   p.sq_b = a.sq[0];
   p.sq_h = a.sq[1];
   p.sq_t = a.sq[2];
-  p.page_table = a.page_table;
-  p.pt_stride = a.pt_stride;
+  p.page_table = table;
+  p.pt_stride = pt_stride;
   p.max_pages = a.max_pages;
   p.seq_lens = a.seq_lens;
   p.cur_lens = a.cur_lens;
@@ -703,19 +920,17 @@ int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream) {
   p.B = a.B;
   p.H = a.H;
   p.T = a.T;
-  p.num_blocks = a.num_blocks;
+  p.num_blocks = num_blocks;
   p.scale_log2 = a.scale * kLog2e;
   p.status = a.status;
-  const PrefillPlan plan = make_prefill_plan(a.B, a.H, a.T, a.D, a.max_pages, BS, a.dtype);
   p.kt_per_split = plan.kt_per_split;
   p.nsplit_max = plan.nsplit_max;
   p.bm = C::BM;
   p.part_o = nullptr;
   p.part_ml = nullptr;
-  if (plan.bytes > 0) {
-    if (!a.workspace || a.workspace_bytes < plan.bytes)
-      return set_error(B2PA_ERR_WORKSPACE, "paged_prefill: workspace of %zu bytes, %zu needed", a.workspace_bytes,
-                       plan.bytes);
+  p.range_flag = range_flag;
+  p.epoch = epoch;
+  if (plan.nsplit_max > 1) {
     p.part_ml = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + plan.off_part_ml);
     p.part_o = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + plan.off_part_o);
   }

@@ -117,10 +117,15 @@ def test_workspace_size_is_monotone(lib):
     assert 0 < a <= b
     assert c > 0 and c % 256 == 0
     assert f(0, 8, 64, 65, 16, 0) == 0
-    # fp32 register-tiled path: at most 8 key tiles (512 keys) per CTA
-    assert lib.b2pa_paged_prefill_workspace_size(8, 8, 256, 64, 32, 16, 0) == 0     # 512 keys: no split
-    n = lib.b2pa_paged_prefill_workspace_size(8, 8, 256, 64, 64, 16, 0)             # 1024 keys: 2 splits
-    assert n >= 8 * 8 * 256 * 2 * (64 + 2) * 4 and n % 256 == 0
+    # fp32, head_dim 64 (tensor cores on bf16 hi/lo splits): the split copies
+    # of K and V (B * max_pages slots x H pages x block x 2D bf16) + the slot table
+    n = lib.b2pa_paged_prefill_workspace_size(8, 8, 256, 64, 32, 16, 0)
+    assert n >= 2 * (8 * 32) * 8 * 16 * (2 * 64) * 2 + 4 * 8 * 32 and n % 256 == 0
+    assert lib.b2pa_paged_prefill_workspace_size(8, 8, 256, 64, 0, 16, 0) == 0      # no pages: no copy
+    # fp32, head_dim 128 (register-tiled path): at most 8 key tiles (512 keys) per CTA
+    assert lib.b2pa_paged_prefill_workspace_size(8, 8, 256, 128, 32, 16, 0) == 0    # 512 keys: no split
+    n = lib.b2pa_paged_prefill_workspace_size(8, 8, 256, 128, 64, 16, 0)            # 1024 keys: 2 splits
+    assert n >= 8 * 8 * 256 * 2 * (128 + 2) * 4 and n % 256 == 0
     assert lib.b2pa_paged_prefill_workspace_size(8, 8, 256, 32, 64, 16, 0) == 0     # head_dim 32: general kernel
     assert lib.b2pa_paged_prefill_workspace_size(8, 8, 256, 64, 65, 16, 1) == 0  # bf16 config[2]: one wave, no split
     assert lib.b2pa_paged_prefill_workspace_size(1, 8, 256, 64, 65, 16, 1) > 0   # one sequence: key-range split

@@ -155,3 +155,35 @@ def test_prefill_tensor_core_key_split(cuda_device, D):
                                prefixes=[1500, 20], curs=[200, 130], seed=5 + D)
     _check(out, ref, torch.bfloat16)
     assert b2pa.read_status(cuda_device) == 0
+
+
+@pytest.mark.parametrize("where", ["k", "v", "q"])
+def test_prefill_f32_outside_split_range_is_recomputed(cuda_device, where):
+    """fp32 head_dim 64 runs on the tensor cores with fp16 hi/lo splits of its
+    operands, which hold |x| < 2^15 only; an input at or beyond that (in K, V
+    or q) sends the call to the fp32 CUDA-core kernel, so the result still
+    matches the oracle."""
+    rng = np.random.default_rng(17)
+    gen = torch.Generator().manual_seed(17)
+    B, H, D, bs, T = 3, 2, 64, 16, 40
+    prefixes, curs = [30, 0, 90], [40, 25, 40]
+    lens = [p + c for p, c in zip(prefixes, curs)]
+    NB = sum(-(-L // bs) for L in lens) + 2
+    kp = torch.randn(NB, H, bs, D, generator=gen) * 0.01
+    vp = torch.randn(NB, H, bs, D, generator=gen)
+    tables = random_tables(rng, lens, NB, bs)
+    q = strided_q(B, H, T, D, torch.float32, "cpu", gen) * 0.01
+    big = 4.0e4
+    if where == "k":
+        kp[tables[2][1], 1, 3, 5] = big  # one key entry of a visible page
+    elif where == "v":
+        vp[tables[0][0], 0, 7, 60] = -big
+    else:
+        q[1, 0, 2, 11] = big
+    kp, vp, q = kp.to(cuda_device), vp.to(cuda_device), q.to(cuda_device)
+    cache = build_cache(b2pa, kp, vp, tables, lens, bs)
+    out = b2pa.paged_attention("b200_paged", q, cache, torch.tensor(curs))
+    ref = orc.paged_attention_c(q.cpu().numpy(), kp.cpu().numpy(), vp.cpu().numpy(), tables, lens, curs)
+    _check(out, ref, torch.float32)
+    assert np.isfinite(out.cpu().numpy()).all()
+    assert b2pa.read_status(cuda_device) == 0
