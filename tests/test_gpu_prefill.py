@@ -111,9 +111,11 @@ def test_prefill_tensor_core_multi_tile(cuda_device, dtype, D):
 
 @pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("bs", [8, 16, 32])
-def test_prefill_f32_tiled_multi_tile(cuda_device, D, bs):
-    # fp32 register-tiled kernel: several 64-row query tiles and 64-key tiles,
-    # a short and an empty sequence, rows padded past cur_len
+def test_prefill_f32_multi_tile(cuda_device, D, bs):
+    # fp32 kernels -- head_dim 64: tensor cores on fp16 hi/lo splits (here
+    # with a key-range split and its combine); 128: register-tiled CUDA cores
+    # -- several query and key tiles, a short and an empty sequence, rows
+    # padded past cur_len
     out, ref = _random_prefill(cuda_device, B=4, H=3, D=D, bs=bs, T=200, dtype=torch.float32,
                                prefixes=[0, 333, 1000, 0], curs=[200, 97, 200, 0], seed=D + bs)
     _check(out, ref, torch.float32)
