@@ -210,7 +210,7 @@ __device__ __forceinline__ int prefill_checked_block(const PfTcParams& p, int ra
   return raw;
 }
 
-// fp32 pools take the split (hi/lo bf16) variant of the kernel.
+// fp32 pools take the split (fp16 hi/lo) variant of the kernel.
 template <typename T>
 constexpr bool kPfSplit = std::is_same<T, float>::value;
 
@@ -789,7 +789,7 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(PfTcParams p) {
 
 // The fp32 variant's first step: copies every page that the prefill of
 // sequence b reads (pages holding keys below min(seq_len, table width)) of K
-// and of V into the workspace as bf16 hi/lo rows -- row (slot * H + h) * BS
+// and of V into the workspace as fp16 hi/lo rows -- row (slot * H + h) * BS
 // + r holds hi in columns [0, D) and lo in [D, 2D), slot = b * max_pages +
 // page -- and writes the slot table the kernel walks in place of the block
 // table: -1 for a page it must not read (past the sequence, a negative

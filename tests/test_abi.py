@@ -117,8 +117,8 @@ def test_workspace_size_is_monotone(lib):
     assert 0 < a <= b
     assert c > 0 and c % 256 == 0
     assert f(0, 8, 64, 65, 16, 0) == 0
-    # fp32, head_dim 64 (tensor cores on bf16 hi/lo splits): the split copies
-    # of K and V (B * max_pages slots x H pages x block x 2D bf16) + the slot table
+    # fp32, head_dim 64 (tensor cores on fp16 hi/lo splits): the split copies
+    # of K and V (B * max_pages slots x H pages x block x 2D halves) + the slot table
     n = lib.b2pa_paged_prefill_workspace_size(8, 8, 256, 64, 32, 16, 0)
     assert n >= 2 * (8 * 32) * 8 * 16 * (2 * 64) * 2 + 4 * 8 * 32 and n % 256 == 0
     assert lib.b2pa_paged_prefill_workspace_size(8, 8, 256, 64, 0, 16, 0) == 0      # no pages: no copy
