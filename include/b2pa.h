@@ -192,14 +192,25 @@ B2PA_API int b2pa_paged_decode_noalloc(const void* q, const int64_t q_strides[4]
                       int B, int H, int D, int block_size, float scale, int dtype,
                       int32_t* status, void* stream);
 
-/* Workspace bytes b2pa_paged_prefill needs (0 for the paths that need none). */
+/*
+ * Workspace bytes b2pa_paged_prefill needs (0 for the paths that need none).
+ * bf16/fp16, and fp32 with head_dim 128: the split-K partials when the key
+ * range is split (small batches).  fp32 with head_dim 64 (tensor cores on
+ * fp16 hi/lo splits of the operands): also the split copies of the pages
+ * the call may read -- B * max_pages * H * block_size * D * 8 bytes, the
+ * size of those fp32 K and V pages -- and a small slot table.
+ */
 B2PA_API size_t b2pa_paged_prefill_workspace_size(int B, int H, int T, int D, int max_pages,
                                          int block_size, int dtype);
 
 /*
  * Chunked-prefill paged attention (any T >= 1, padded rows included).
  * Replaces paged_attention_prefill_triton,
- * src/kernels/triton_paged_attention.py:220-258.
+ * src/kernels/triton_paged_attention.py:220-258.  fp32 results match fp32
+ * arithmetic to the fp32 tolerance on every path; with head_dim 64 the call
+ * runs on the tensor cores unless an input has magnitude >= 2^15 or is not
+ * finite, in which case a CUDA-core kernel recomputes it (same results,
+ * slower).
  */
 B2PA_API int b2pa_paged_prefill(const void* q, const int64_t q_strides[4],
                        const void* k_pool, const void* v_pool,
