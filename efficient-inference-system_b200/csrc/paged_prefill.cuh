@@ -76,7 +76,10 @@ struct PrefillSmem {
 template <typename T, int D, int BS>
 __global__ void __launch_bounds__(kPfThreads) paged_prefill_simt_kernel(PrefillParams p) {
   using S = PrefillSmem<D>;
-  if (p.run_if != nullptr && *p.run_if != p.run_epoch) return;  // a backup launch with nothing to redo
+  if (p.run_if != nullptr) {  // a backup launch (programmatic): nothing to redo unless the flag says so
+    pdl_wait();
+    if (*p.run_if != p.run_epoch) return;
+  }
   extern __shared__ __align__(16) float psm[];
   float* Qs = psm;
   float* Ks = Qs + S::Q_FLOATS;
@@ -252,7 +255,12 @@ int launch_prefill_simt(const AttnArgs& a, cudaStream_t stream, const uint32_t* 
   if (rc_attr != B2PA_OK) return rc_attr;
   cudaError_t e;
   dim3 grid((a.T + kPfTQ - 1) / kPfTQ, a.H, a.B);
-  kern<<<grid, kPfThreads, smem, stream>>>(p);
+  if (run_if != nullptr) {
+    e = launch_pdl(kern, grid, dim3(kPfThreads), smem, stream, p);
+    if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill launch: %s", cudaGetErrorString(e));
+  } else {
+    kern<<<grid, kPfThreads, smem, stream>>>(p);
+  }
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill launch: %s", cudaGetErrorString(e));
   return B2PA_OK;
