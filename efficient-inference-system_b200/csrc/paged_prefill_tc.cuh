@@ -260,11 +260,12 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
   int* sblk = reinterpret_cast<int*>(smem + C::OFF_BLK);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Launched programmatically after the kernel before it (the KV append of
+  // the step, or the fp32 variant's pre-pass): wait for its results before
+  // reading anything; let the next kernel launch behind this grid.
+  pdl_wait();
+  pdl_launch_dependents();
   if constexpr (SPLIT) {
-    // Launched programmatically after the pre-pass: wait for its split pages,
-    // slot table and range flag; let the backup launch behind this grid.
-    pdl_wait();
-    pdl_launch_dependents();
     // an input out of the split's range was seen (pre-pass or another CTA):
     // the CUDA-core kernel that follows recomputes the call.  One read,
     // shared, so the whole CTA takes the same branch.
@@ -950,12 +951,8 @@ int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream, uint32_t epoch = 0
   if (rc_attr != B2PA_OK) return rc_attr;
   cudaError_t e;
   dim3 grid(((a.T + C::BM - 1) / C::BM) * plan.nsplit_max, a.H, a.B);
-  if constexpr (SPLIT) {
-    e = launch_pdl(kern, grid, dim3(C::THREADS), smem, stream, tmk, tmv, p);
-    if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill_tc launch: %s", cudaGetErrorString(e));
-  } else {
-    kern<<<grid, C::THREADS, smem, stream>>>(tmk, tmv, p);
-  }
+  e = launch_pdl(kern, grid, dim3(C::THREADS), smem, stream, tmk, tmv, p);
+  if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill_tc launch: %s", cudaGetErrorString(e));
   if (plan.nsplit_max > 1) {
     const int64_t rows = (int64_t)a.B * a.H * a.T;
     prefill_combine_kernel<T, D, BS><<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(p);
