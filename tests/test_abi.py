@@ -109,6 +109,21 @@ def test_decode_append_argument_validation(lib):
     assert _decode_append(lib, B=0) == 0                             # empty batch: nothing to do
 
 
+def test_prefill_f32_split_needs_its_workspace(lib):
+    """fp32 head_dim 64 prefill runs on split copies of the pages held in the
+    workspace: a missing or short workspace is refused before any launch."""
+    i64 = lambda t: (ctypes.c_int64 * 4)(*t)
+    B, H, T, D, bs, mp = 2, 2, 8, 64, 16, 4
+    need = lib.b2pa_paged_prefill_workspace_size(B, H, T, D, mp, bs, 0)
+    assert need > 0
+    qs = (T * H * D, D, H * D, 1)
+    args = [4096, i64(qs), 16, 16, i64((H * bs * D, bs * D, D, 1)), 10, 8, mp, mp, 8, 8, 8192, i64(qs),
+            B, H, T, D, bs, 0.125, 0]
+    assert lib.b2pa_paged_prefill(*args, None, 0, None, None) == -4
+    assert lib.b2pa_paged_prefill(*args, 256, need - 256, None, None) == -4
+    assert "workspace" in _lib.last_error()
+
+
 def test_workspace_size_is_monotone(lib):
     f = lib.b2pa_paged_decode_workspace_size
     a = f(64, 8, 64, 65, 16, 0)
