@@ -180,7 +180,7 @@ def block_table_and_lengths(cache, device: torch.device, extra: list[list[int]] 
         pass
     if extra:
         for i, row in enumerate(extra):
-            small[B * (i + 1): B * (i + 2)] = row
+            small[B * (i + 1): B * (i + 2)] = row  # a list, an array, or a scalar for equal values
     n_pairs = len(cells) // 2 if cells is not None else 0
     if ent.dev_table is not None and changed and 0 < n_pairs <= _MAX_PATCH_PAIRS:
         # few cells changed: send (index, value) pairs with the small rows and

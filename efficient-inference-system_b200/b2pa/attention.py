@@ -99,13 +99,15 @@ def paged_attention(backend: str, q: torch.Tensor, kv_cache, current_lengths) ->
         raise RuntimeError("b2pa: q must be a CUDA tensor (this package has no CPU path)")
     B, _, T, _ = q.shape
     dev = q.device
+    # host-side current lengths as one int32 metadata row (a scalar stands for
+    # a row of equal values)
     host_cur = None
     if current_lengths is None:
-        host_cur = [T] * B
+        host_cur = T
     elif isinstance(current_lengths, int):
-        host_cur = [current_lengths] * B
+        host_cur = current_lengths
     elif isinstance(current_lengths, torch.Tensor) and not current_lengths.is_cuda:
-        host_cur = [int(x) for x in current_lengths.tolist()]
+        host_cur = current_lengths.numpy()
     elif isinstance(current_lengths, (list, tuple)):
         host_cur = [int(x) for x in current_lengths]
     pool = kv_cache.pool

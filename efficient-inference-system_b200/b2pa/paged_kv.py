@@ -247,9 +247,11 @@ _pool_of = operator.attrgetter("pool")
 _SMALL_BATCH = 64  # below this, plain Python loops beat numpy's per-call overhead
 
 
-def plan_append(cache, k_new: torch.Tensor, lengths) -> list[int]:
+def plan_append(cache, k_new: torch.Tensor, lengths, as_array: bool = False):
     """Initialises the pool and allocates blocks request by request, in batch
-    order (paged_kv.py:165-171); returns each request's start position.
+    order (paged_kv.py:165-171); returns each request's start position (a
+    list; for large batches with ``as_array`` the int64 array it was computed
+    in, which the launch metadata takes without a conversion).
 
     For large batches the per-request arithmetic is vectorised and only
     requests whose write crosses into new blocks (one in ``block_size`` per
@@ -308,7 +310,7 @@ def plan_append(cache, k_new: torch.Tensor, lengths) -> list[int]:
         ends = (start + n).tolist()
         for b in grown.tolist():
             states[b].seq_len = ends[b]
-    return start.tolist()
+    return start if as_array else start.tolist()
 
 
 def append_batch_into(cache, k_new: torch.Tensor, v_new: torch.Tensor, current_lengths=None) -> torch.Tensor:
@@ -331,7 +333,7 @@ def append_batch_into(cache, k_new: torch.Tensor, v_new: torch.Tensor, current_l
     pool = cache.pool
     if getattr(pool, "_b2pa_pending", None) is not None:
         flush_pending(pool)  # an earlier deferred append goes first
-    starts = plan_append(cache, k_new, clamped)
+    starts = plan_append(cache, k_new, clamped, as_array=True)
     if any_new and k_new.device.type == "cuda":
         if _fused_append and T == 1 and k_new.stride(3) == 1 and v_new.stride(3) == 1:
             seq_out = torch.empty(B, dtype=torch.long, device=k_new.device)
