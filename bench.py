@@ -646,29 +646,36 @@ def main_secondary(args) -> int:
         torch.cuda.synchronize()
         _lib.raise_on_device_status(dev, "secondary bench")
         step_ms = float(np.mean([a.elapsed_time(c) for a, _, c in ev]))
-        fused_ms = None
-        if T == 1:
-            # the same step as one b2pa_paged_decode_append call
-            def fused():
+        # the same step as one call: b2pa_paged_decode_append (T == 1) or
+        # b2pa_paged_prefill_append (the chunk's append inside the fp32
+        # tensor-core path's page copy; append kernel + prefill otherwise)
+        def fused():
+            if T == 1:
                 _lib.check(lib.b2pa_paged_decode_append(
                     q.data_ptr(), _lib.strides4(q), kn.data_ptr(), _lib.strides4(kn), vn.data_ptr(),
                     _lib.strides4(vn), kp.data_ptr(), vp.data_ptr(), _lib.strides4(kp), NB, pt.data_ptr(),
                     max_pages, max_pages, seq.data_ptr(), cur.data_ptr(), start.data_ptr(), cur.data_ptr(), None,
                     out.data_ptr(), _lib.strides4(out), B, Hs, Ds, bs, scale, dt, ws.data_ptr(), ws.numel(),
                     status, sh), "decode_append")
+            else:
+                _lib.check(lib.b2pa_paged_prefill_append(
+                    q.data_ptr(), _lib.strides4(q), kn.data_ptr(), _lib.strides4(kn), vn.data_ptr(),
+                    _lib.strides4(vn), kp.data_ptr(), vp.data_ptr(), _lib.strides4(kp), NB, pt.data_ptr(),
+                    max_pages, max_pages, seq.data_ptr(), cur.data_ptr(), start.data_ptr(), cur.data_ptr(), None,
+                    out.data_ptr(), _lib.strides4(out), B, Hs, T, Ds, bs, scale, dt, ws.data_ptr(), ws.numel(),
+                    status, sh), "prefill_append")
 
-            for _ in range(max(args.warmup, 3)):
-                fused()
-            fev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-                   for _ in range(args.steps)]
-            for e0, e1 in fev:
-                flush.zero_()
-                e0.record()
-                fused()
-                e1.record()
-            torch.cuda.synchronize()
-            _lib.raise_on_device_status(dev, "secondary bench (fused)")
-            fused_ms = float(np.mean([a.elapsed_time(b) for a, b in fev]))
+        for _ in range(max(args.warmup, 3)):
+            fused()
+        fev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+        for e0, e1 in fev:
+            flush.zero_()
+            e0.record()
+            fused()
+            e1.record()
+        torch.cuda.synchronize()
+        _lib.raise_on_device_status(dev, "secondary bench (fused)")
+        fused_ms = float(np.mean([a.elapsed_time(b) for a, b in fev]))
         attn_eager_ms = float(np.mean([b.elapsed_time(c) for _, b, c in ev]))
         # Device time without host launch gaps: the attention call captured in
         # a CUDA graph and replayed (L2 flushed before every replay).
@@ -702,7 +709,10 @@ def main_secondary(args) -> int:
         if T > 1:
             flops = _prefill_flops(prefix, T, Hs, Ds)
             bytes_ = kv_bytes + 2 * B * Hs * T * Ds * es
-            line.update({"tokens_per_s": B * T / (step_ms / 1e3), "attention_tflops": flops / (attn_ms / 1e3) / 1e12,
+            line.update({"tokens_per_s": B * T / (step_ms / 1e3),
+                         "ms_per_step_fused_append_prefill": fused_ms,
+                         "tokens_per_s_fused": B * T / (fused_ms / 1e3),
+                         "attention_tflops": flops / (attn_ms / 1e3) / 1e12,
                          "flops_per_launch": flops, "bytes_per_launch": bytes_,
                          "attention_hbm_gbs": bytes_ / (attn_ms / 1e3) / 1e9,
                          "frac_of_bf16_tensor_peak": flops / (attn_ms / 1e3) / 1e12 / peaks["bf16_tflops"],

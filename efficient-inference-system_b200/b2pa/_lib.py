@@ -53,6 +53,9 @@ SIGNATURES: dict[str, tuple] = {
     "b2pa_paged_prefill_workspace_size": (ctypes.c_size_t, [_I, _I, _I, _I, _I, _I, _I]),
     "b2pa_paged_prefill": (_I, [_VP, _I64P, _VP, _VP, _I64P, _I64, _VP, _I64, _I, _VP, _VP, _VP, _I64P,
                                 _I, _I, _I, _I, _I, ctypes.c_float, _I, _VP, ctypes.c_size_t, _VP, _VP]),
+    "b2pa_paged_prefill_append": (_I, [_VP, _I64P, _VP, _I64P, _VP, _I64P, _VP, _VP, _I64P, _I64, _VP, _I64, _I,
+                                       _VP, _VP, _VP, _VP, _VP, _VP, _I64P, _I, _I, _I, _I, _I, ctypes.c_float,
+                                       _I, _VP, ctypes.c_size_t, _VP, _VP]),
     "b2pa_zero_blocks": (_I, [_VP, _VP, _I64P, _I64, _VP, _I, _I, _I, _I, _I, _VP, _VP]),
     "b2pa_patch_table": (_I, [_VP, _I64, _VP, _I, _VP, _VP]),
     "b2pa_selftest_wait_timeout": (_I, [_VP, _VP, _VP]),

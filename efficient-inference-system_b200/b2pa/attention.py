@@ -113,8 +113,11 @@ def paged_attention(backend: str, q: torch.Tensor, kv_cache, current_lengths) ->
     pool = kv_cache.pool
     pend = getattr(pool, "_b2pa_pending", None)
     if pend is not None:
-        if pend.cache is kv_cache and T == 1 and pend.k_new.device == dev and pool.k_blocks.dtype == q.dtype:
-            return _decode_with_append(q, kv_cache, current_lengths, host_cur, take_pending(pool))
+        if (pend.cache is kv_cache and pend.k_new.shape[2] == T and pend.k_new.device == dev
+                and pool.k_blocks.dtype == q.dtype):
+            if T == 1:
+                return _decode_with_append(q, kv_cache, current_lengths, host_cur, take_pending(pool))
+            return _prefill_with_append(q, kv_cache, current_lengths, host_cur, take_pending(pool))
         flush_pending(pool)
     if pool.k_blocks is None:
         # Nothing was ever appended to this layer: every row sees no key, which
@@ -169,4 +172,45 @@ def _decode_with_append(q, kv_cache, current_lengths, host_cur, pend) -> torch.T
         if rc == _lib.STATUS_CODES["B2PA_ERR_UNSUPPORTED"]:
             return _attn_call("decode", q, kb, vb, page_table, seq_lens, cur, max_pages)
         raise RuntimeError(f"b2pa_paged_decode_append failed: {_lib.STATUS_NAMES.get(rc, rc)}: {err}")
+    return out
+
+
+def _prefill_with_append(q, kv_cache, current_lengths, host_cur, pend) -> torch.Tensor:
+    """Chunked prefill of ``q`` with the deferred append ``pend`` of the same
+    batch (b2pa_paged_prefill_append): for fp32 pools with head_dim 64 the
+    append happens inside the page copy of the tensor-core path, otherwise
+    the append kernel runs first."""
+    pool = kv_cache.pool
+    kb, vb = pool.k_blocks, pool.v_blocks
+    dev = q.device
+    B, H, T, D = q.shape
+    if host_cur is not None:
+        page_table, seq_lens, cur, start_t, len_t, max_pages = block_table_and_lengths(
+            kv_cache, dev, [host_cur, pend.starts, pend.lengths], transient=True)
+    else:
+        page_table, seq_lens, start_t, len_t, max_pages = block_table_and_lengths(
+            kv_cache, dev, [pend.starts, pend.lengths], transient=True)
+        cur = current_lengths.to(dtype=torch.int32)
+    out = torch.empty_like(q)
+    dt = _lib.dtype_code(q.dtype)
+    lib = _lib.load()
+    block_size = kb.shape[2]
+    ws_bytes = lib.b2pa_paged_prefill_workspace_size(B, H, T, D, max_pages, block_size, dt)
+    ws = _lib.workspace(dev, ws_bytes) if ws_bytes else None
+    k_new, v_new = pend.k_new, pend.v_new
+    rc = lib.b2pa_paged_prefill_append(
+        q.data_ptr(), _lib.strides4(q), k_new.data_ptr(), _lib.strides4(k_new), v_new.data_ptr(),
+        _lib.strides4(v_new), kb.data_ptr(), vb.data_ptr(), _lib.strides4(kb), kb.shape[0],
+        page_table.data_ptr() if max_pages else None, page_table.stride(0), max_pages,
+        seq_lens.data_ptr(), cur.data_ptr(), start_t.data_ptr(), len_t.data_ptr(), pend.seq_out.data_ptr(),
+        out.data_ptr(), _lib.strides4(out), B, H, T, D, block_size, 1.0 / math.sqrt(D), dt,
+        ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
+        _lib.status_buffer(dev).data_ptr(), _lib.stream_handle(dev))
+    if rc != 0:
+        # Nothing was launched: append with the ordinary kernel so the pool
+        # ends as the reference's append leaves it, then report.
+        err = _lib.last_error()
+        seq = _kv_append(kv_cache, k_new, v_new, pend.starts, pend.lengths)
+        pend.seq_out.copy_(seq)
+        raise RuntimeError(f"b2pa_paged_prefill_append failed: {_lib.STATUS_NAMES.get(rc, rc)}: {err}")
     return out

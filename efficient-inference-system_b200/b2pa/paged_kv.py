@@ -335,7 +335,7 @@ def append_batch_into(cache, k_new: torch.Tensor, v_new: torch.Tensor, current_l
         flush_pending(pool)  # an earlier deferred append goes first
     starts = plan_append(cache, k_new, clamped, as_array=True)
     if any_new and k_new.device.type == "cuda":
-        if _fused_append and T == 1 and k_new.stride(3) == 1 and v_new.stride(3) == 1:
+        if _fused_append and k_new.stride(3) == 1 and v_new.stride(3) == 1:
             seq_out = torch.empty(B, dtype=torch.long, device=k_new.device)
             try:
                 pool._b2pa_pending = _PendingAppend(cache, k_new, v_new, starts, clamped, seq_out)
@@ -347,24 +347,26 @@ def append_batch_into(cache, k_new: torch.Tensor, v_new: torch.Tensor, current_l
     return torch.tensor([s.seq_len for s in cache.states], dtype=torch.long, device=k_new.device)
 
 
-# --------------------------------------------- deferred (fused) decode append
-# With the fused append on, a decode-step append_batch (T == 1) allocates its
-# blocks and advances seq_len on the host as usual, but leaves the K/V row
-# copy pending on the pool; the paged_attention call that follows on the
-# same batch object -- the reference's order, src/model/attention.py:56-62 --
-# performs it inside its decode launch (b2pa_paged_decode_append), one launch
-# where there were two.  Every other b2pa call that touches the pool first
-# performs a pending copy with the ordinary append kernel.
+# ------------------------------------------------------ deferred (fused) append
+# With the fused append on, append_batch allocates its blocks and advances
+# seq_len on the host as usual, but leaves the K/V row copy pending on the
+# pool; the paged_attention call that follows on the same batch object --
+# the reference's order, src/model/attention.py:56-62 -- performs it in its
+# own launches: inside the decode launch (b2pa_paged_decode_append) for a
+# decode step, inside the page copy of the fp32 tensor-core prefill
+# (b2pa_paged_prefill_append) for a prompt chunk.  Every other b2pa call that
+# touches the pool first performs a pending copy with the ordinary append
+# kernel.
 _fused_append = False
 
 
 def set_fused_append(enabled: bool) -> bool:
-    """Turns the deferred, fused decode append on or off for the process;
-    returns the previous setting.  Off by default.
+    """Turns the deferred, fused append on or off for the process; returns
+    the previous setting.  Off by default.
 
-    While it is on, the pool bytes of the last decode-step append_batch on a
-    pool (and the int64 lengths it returned) are written by the next b2pa
-    call on that pool: normally the paged_attention of the same batch.  Code
+    While it is on, the pool bytes of the last append_batch on a pool (and
+    the int64 lengths it returned) are written by the next b2pa call on that
+    pool: normally the paged_attention of the same batch.  Code
     that reads pool tensors directly in between, or releases or allocates
     blocks through objects other than this package's, must call
     ``flush_pending(pool)`` first."""

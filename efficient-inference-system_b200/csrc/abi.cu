@@ -317,7 +317,7 @@ AttnArgs make_attn_args(const void* q, const int64_t* qs, const void* k_pool, co
   a.workspace_bytes = workspace_bytes;
   a.status = status;
   a.k_new = a.v_new = nullptr;
-  a.skn[0] = a.skn[1] = a.svn[0] = a.svn[1] = 0;
+  a.skn[0] = a.skn[1] = a.skn[2] = a.svn[0] = a.svn[1] = a.svn[2] = 0;
   a.app_start = a.app_len = nullptr;
   a.app_vb = 0;
   a.seq_out = nullptr;
@@ -511,6 +511,58 @@ int b2pa_paged_prefill(const void* q, const int64_t q_strides[4], const void* k_
     case B2PA_DTYPE_BF16: return launch_paged_prefill_bf16(a, s);
     default: return launch_paged_prefill_f16(a, s);
   }
+}
+
+int b2pa_paged_prefill_append(const void* q, const int64_t q_strides[4], const void* k_new,
+                              const int64_t new_k_strides[4], const void* v_new, const int64_t new_v_strides[4],
+                              void* k_pool, void* v_pool, const int64_t pool_strides[4], int64_t num_blocks,
+                              const int32_t* page_table, int64_t pt_stride, int max_pages, const int32_t* seq_lens,
+                              const int32_t* cur_lens, const int32_t* start_pos, const int32_t* lengths,
+                              int64_t* seq_lens_out, void* out, const int64_t out_strides[4], int B, int H, int T,
+                              int D, int block_size, float scale, int dtype, void* workspace, size_t workspace_bytes,
+                              int32_t* status, void* stream) {
+  int rc = validate_attention("paged_prefill_append", q, q_strides, k_pool, v_pool, pool_strides, num_blocks,
+                              page_table, pt_stride, max_pages, seq_lens, cur_lens, out, out_strides, B, H, T, D,
+                              block_size, dtype);
+  if (rc != B2PA_OK || B == 0 || T == 0) return rc;
+  if (T > 65535 * 32) return set_error(B2PA_ERR_UNSUPPORTED, "paged_prefill_append: T=%d too large", T);
+  if (!k_new || !v_new || !new_k_strides || !new_v_strides || !start_pos || !lengths)
+    return set_error(B2PA_ERR_INVALID_ARGUMENT, "paged_prefill_append: null pointer argument");
+  if (new_k_strides[3] != 1 || new_v_strides[3] != 1)
+    return set_error(B2PA_ERR_UNSUPPORTED, "paged_prefill_append: k_new/v_new need a unit head_dim stride");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  AttnArgs a = make_attn_args(q, q_strides, k_pool, v_pool, num_blocks, page_table, pt_stride, max_pages, seq_lens,
+                              cur_lens, out, out_strides, B, H, T, D, block_size, scale, dtype, workspace,
+                              workspace_bytes, status);
+  // The fp32 split path copies every page the call reads anyway: its pre-pass
+  // takes the new rows from k_new / v_new (16-byte rows) and writes them into
+  // the pool as well.  Every other path appends first, with the append kernel.
+  const int es = dtype_size(dtype);
+  bool rows16 = aligned_to(k_new, 16) && aligned_to(v_new, 16);
+  for (int i = 0; i < 3; ++i) rows16 = rows16 && (new_k_strides[i] * es) % 16 == 0 && (new_v_strides[i] * es) % 16 == 0;
+  if (dtype == B2PA_DTYPE_F32 && rows16 &&
+      make_prefill_plan(B, H, T, D, max_pages, block_size, dtype).split_tc) {
+    a.k_new = k_new;
+    a.v_new = v_new;
+    for (int i = 0; i < 3; ++i) {
+      a.skn[i] = new_k_strides[i];
+      a.svn[i] = new_v_strides[i];
+    }
+    a.app_start = start_pos;
+    a.app_len = lengths;
+    a.seq_out = seq_lens_out;
+    return launch_paged_prefill_f32(a, s);
+  }
+  rc = b2pa_kv_append(k_new, new_k_strides, v_new, new_v_strides, k_pool, v_pool, pool_strides, num_blocks, page_table,
+                      pt_stride, max_pages, start_pos, lengths, B, H, T, D, block_size, dtype, status, stream);
+  if (rc != B2PA_OK) return rc;
+  switch (dtype) {
+    case B2PA_DTYPE_F32: rc = launch_paged_prefill_f32(a, s); break;
+    case B2PA_DTYPE_BF16: rc = launch_paged_prefill_bf16(a, s); break;
+    default: rc = launch_paged_prefill_f16(a, s); break;
+  }
+  if (rc != B2PA_OK) return rc;
+  return launch_copy_lengths(seq_lens, seq_lens_out, B, s);
 }
 
 int b2pa_zero_blocks(void* k_pool, void* v_pool, const int64_t pool_strides[4], int64_t num_blocks,

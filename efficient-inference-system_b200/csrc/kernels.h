@@ -90,14 +90,15 @@ struct AttnArgs {
   void* workspace;
   size_t workspace_bytes;
   int32_t* status;
-  // KV append fused into the decode launch (b2pa_paged_decode_append); unused
-  // when app_len is null.  For each b with app_len[b] > 0, row 0 of
-  // k_new/v_new ([B,H,1,D], element strides skn/svn of B and H, unit D
-  // stride) is written at position app_start[b]; app_vb is the byte width of
-  // the row copy's accesses.  seq_out (optional) receives seq_lens as int64.
+  // KV append fused into the attention launch (b2pa_paged_decode_append,
+  // b2pa_paged_prefill_append); unused when app_len is null.  For each b,
+  // rows t < min(app_len[b], T) of k_new/v_new ([B,H,T,D], element strides
+  // skn/svn of B, H and T, unit D stride) are written at positions
+  // app_start[b] + t; app_vb is the byte width of the decode's row copy.
+  // seq_out (optional) receives seq_lens as int64.
   const void* k_new;
   const void* v_new;
-  int64_t skn[2], svn[2];
+  int64_t skn[3], svn[3];
   const int32_t* app_start;
   const int32_t* app_len;
   int app_vb;
@@ -105,6 +106,7 @@ struct AttnArgs {
 };
 
 int launch_kv_append(const AppendArgs& a, cudaStream_t stream);
+int launch_copy_lengths(const int32_t* seq_lens, int64_t* out, int B, cudaStream_t stream);
 int launch_zero_blocks(const ZeroArgs& a, cudaStream_t stream);
 int launch_patch_table(int32_t* table, int64_t n_cells, const int32_t* pairs, int n_pairs, int32_t* status,
                        cudaStream_t stream);

@@ -114,6 +114,21 @@ __global__ void __launch_bounds__(256) zero_blocks_kernel(ZeroArgs a, int64_t bl
   }
 }
 
+// seq_lens as int64 (the lengths append_batch returns), for the fused
+// append + prefill entry when it runs as separate launches.
+__global__ void __launch_bounds__(256) copy_lengths_kernel(const int32_t* seq_lens, int64_t* out, int B) {
+  pdl_wait();
+  for (int b = blockIdx.x * blockDim.x + threadIdx.x; b < B; b += gridDim.x * blockDim.x) out[b] = seq_lens[b];
+}
+
+int launch_copy_lengths(const int32_t* seq_lens, int64_t* out, int B, cudaStream_t stream) {
+  if (B <= 0 || out == nullptr) return B2PA_OK;
+  const cudaError_t e = launch_pdl(copy_lengths_kernel, dim3((unsigned)((B + 255) / 256)), dim3(256), 0, stream,
+                                   seq_lens, out, B);
+  if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "copy_lengths launch: %s", cudaGetErrorString(e));
+  return B2PA_OK;
+}
+
 static bool aligned(const void* p, int bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) == 0; }
 
 int launch_kv_append(const AppendArgs& a, cudaStream_t stream) {

@@ -800,8 +800,8 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(PfTcParams p) {
 // table: -1 for a page it must not read (past the sequence, a negative
 // entry, or a block id outside the pool, which is also reported).
 struct PfSplitArgs {
-  const float* k_pool;
-  const float* v_pool;
+  float* k_pool;  // written only by the fused append (rows of k_new / v_new)
+  float* v_pool;
   const int32_t* page_table;
   int64_t pt_stride;
   int max_pages;
@@ -814,6 +814,18 @@ struct PfSplitArgs {
   uint32_t* range_flag;
   uint32_t epoch;
   int32_t* status;
+  // Fused KV append (b2pa_paged_prefill_append; app_len null: none): rows
+  // t < min(app_len[b], T) of k_new / v_new go to positions app_start[b] + t,
+  // which must end at seq_lens[b].  The page copy takes those rows from
+  // k_new / v_new and also writes them into the pool.  seq_out (optional)
+  // receives seq_lens as int64.
+  const float* k_new;
+  const float* v_new;
+  int64_t skn[3], svn[3];
+  const int32_t* app_start;
+  const int32_t* app_len;
+  int T;
+  int64_t* seq_out;
 };
 
 template <int D, int BS>
@@ -834,16 +846,47 @@ __global__ void __launch_bounds__(128) prefill_split_pages_kernel(PfSplitArgs a)
     }
   }
   if (h == 0 && threadIdx.x == 0) a.slots[slot] = (int32_t)(blk >= 0 ? slot : -1);
+  // positions [app_lo, app_hi) of sequence b come from k_new / v_new
+  int64_t app_lo = 0, app_hi = 0;
+  if (a.app_len != nullptr) {
+    int len = a.app_len[b];
+    len = len < a.T ? len : a.T;
+    if (len > 0) {
+      app_lo = a.app_start[b];
+      app_hi = app_lo + len;
+      if (app_lo < 0 || app_hi != (int64_t)a.seq_lens[b]) {  // not the chunk that ends the sequence
+        if (i == 0 && h == 0 && threadIdx.x == 0) set_status(a.status, B2PA_ERR_INVALID_ARGUMENT);
+        app_lo = app_hi = 0;
+      }
+    }
+    if (a.seq_out != nullptr && i == 0 && h == 0 && threadIdx.x == 0) a.seq_out[b] = a.seq_lens[b];
+  }
   if (blk < 0) return;
   const int64_t src = ((blk * a.H + h) * BS) * D;
   const int64_t dst = ((slot * a.H + h) * BS) * (2 * D);
   bool in_range = true;
   for (int idx = threadIdx.x; idx < BS * D / 8; idx += blockDim.x) {
     const int r = idx / (D / 8), c8 = idx - (idx / (D / 8)) * (D / 8);
+    const int64_t pos = (int64_t)i * BS + r;
+    const bool fresh = pos >= app_lo && pos < app_hi;
 #pragma unroll
     for (int kv = 0; kv < 2; ++kv) {
-      const float4* s4 = reinterpret_cast<const float4*>((kv ? a.v_pool : a.k_pool) + src + (int64_t)r * D + c8 * 8);
-      const float4 x0 = s4[0], x1 = s4[1];
+      float* pool_row = (kv ? a.v_pool : a.k_pool) + src + (int64_t)r * D + c8 * 8;
+      float4 x0, x1;
+      if (fresh) {
+        const int64_t t = pos - app_lo;
+        const int64_t* sn = kv ? a.svn : a.skn;
+        const float4* n4 = reinterpret_cast<const float4*>((kv ? a.v_new : a.k_new) + (int64_t)b * sn[0] +
+                                                           (int64_t)h * sn[1] + t * sn[2] + c8 * 8);
+        x0 = n4[0];
+        x1 = n4[1];
+        reinterpret_cast<float4*>(pool_row)[0] = x0;
+        reinterpret_cast<float4*>(pool_row)[1] = x1;
+      } else {
+        const float4* s4 = reinterpret_cast<const float4*>(pool_row);
+        x0 = s4[0];
+        x1 = s4[1];
+      }
       const float f[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
       for (int e = 0; e < 8; ++e) in_range = in_range && fabsf(f[e]) < kSplitRange;
@@ -878,8 +921,18 @@ int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream, uint32_t epoch = 0
     if (!plan.split_tc) return set_error(B2PA_ERR_UNSUPPORTED, "paged_prefill: fp32 split plan not applicable");
     char* ws = static_cast<char*>(a.workspace);
     PfSplitArgs sa;
-    sa.k_pool = static_cast<const float*>(a.k_pool);
-    sa.v_pool = static_cast<const float*>(a.v_pool);
+    sa.k_pool = const_cast<float*>(static_cast<const float*>(a.k_pool));
+    sa.v_pool = const_cast<float*>(static_cast<const float*>(a.v_pool));
+    sa.k_new = static_cast<const float*>(a.k_new);
+    sa.v_new = static_cast<const float*>(a.v_new);
+    for (int i = 0; i < 3; ++i) {
+      sa.skn[i] = a.skn[i];
+      sa.svn[i] = a.svn[i];
+    }
+    sa.app_start = a.app_start;
+    sa.app_len = a.app_len;
+    sa.T = a.T;
+    sa.seq_out = a.seq_out;
     sa.page_table = a.page_table;
     sa.pt_stride = a.pt_stride;
     sa.max_pages = a.max_pages;

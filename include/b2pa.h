@@ -223,6 +223,39 @@ B2PA_API int b2pa_paged_prefill(const void* q, const int64_t q_strides[4],
                        int32_t* status, void* stream);
 
 /*
+ * Chunked prefill with the chunk's KV append in the same call.  Replaces the
+ * pair CausalSelfAttention.forward makes per layer for a prompt chunk
+ * (src/model/attention.py:56-62): BatchedPagedKVCache.append_batch
+ * (src/cache/paged_kv.py:151-172, as b2pa_kv_append) followed by
+ * paged_attention_prefill_triton (src/kernels/triton_paged_attention.py:
+ * 220-258, as b2pa_paged_prefill).  For each b, rows t < min(lengths[b], T)
+ * of k_new / v_new ([B,H,T,D] element strides, unit D stride) go to pool
+ * positions start_pos[b] + t, which must end at seq_lens[b] (the lengths
+ * after the append; where the append is fused, see below, a sequence whose
+ * rows do not is skipped and B2PA_ERR_INVALID_ARGUMENT set in the status
+ * word); the attention of the chunk sees them.
+ * seq_lens_out (may be NULL) receives seq_lens as int64, the value
+ * append_batch returns.  For fp32 pools with head_dim 64 the append happens
+ * inside the launch that copies the pages for the tensor cores; otherwise
+ * the append kernel runs first.  Same workspace as b2pa_paged_prefill.  Pool
+ * bytes and outputs are identical to b2pa_kv_append followed by
+ * b2pa_paged_prefill.
+ */
+B2PA_API int b2pa_paged_prefill_append(const void* q, const int64_t q_strides[4],
+                       const void* k_new, const int64_t new_k_strides[4],
+                       const void* v_new, const int64_t new_v_strides[4],
+                       void* k_pool, void* v_pool,
+                       const int64_t pool_strides[4], int64_t num_blocks,
+                       const int32_t* page_table, int64_t pt_stride, int max_pages,
+                       const int32_t* seq_lens, const int32_t* cur_lens,
+                       const int32_t* start_pos, const int32_t* lengths,
+                       int64_t* seq_lens_out,
+                       void* out, const int64_t out_strides[4],
+                       int B, int H, int T, int D, int block_size, float scale, int dtype,
+                       void* workspace, size_t workspace_bytes,
+                       int32_t* status, void* stream);
+
+/*
  * Zeroes whole blocks of both pools in one launch.  Replaces the per-block
  * k_blocks[id].zero_() / v_blocks[id].zero_() pair of
  * LayerBlockPool.release_block, src/cache/paged_kv.py:80-85.

@@ -10,7 +10,10 @@ and the deferred append_batch that feeds it.
   cur_len 0/1/2/large (a cur_len of 2 hides the new token), split sequences.
 * Bad inputs are reported through the status word without touching memory
   outside the pool.
-* Python: with ``b2pa.set_fused_append(True)`` a decode loop through
+* Chunked prefill with its append (b2pa_paged_prefill_append): pools and
+  outputs bit-identical to b2pa_kv_append + b2pa_paged_prefill, on the fp32
+  tensor-core path (append inside the page copy) and the others.
+* Python: with ``b2pa.set_fused_append(True)`` a prefill + decode loop through
   ``append_batch`` + ``paged_attention`` (the reference's order,
   src/model/attention.py:56-62) gives the same outputs, returned lengths and
   pools as the eager path, including pool growth, a release between the two
@@ -260,3 +263,109 @@ def test_flush_pending_writes_the_row(cuda_device):
             assert torch.equal(pool.v_blocks[s.block_ids[0], :, 0], v[b, :, 0])
     finally:
         b2pa.set_fused_append(prev)
+
+
+# ---------------------------------------------- chunked prefill with its append
+def _prefill_problem(device, *, H, D, bs, T, dtype, prefixes, app, seed):
+    """Pools and table for one prompt chunk per sequence: app[b] <= T new
+    tokens after prefixes[b] cached ones."""
+    rng = np.random.default_rng(seed)
+    gen = torch.Generator().manual_seed(seed)
+    B = len(prefixes)
+    lens_new = [p + a for p, a in zip(prefixes, app)]
+    NB = sum(-(-L // bs) for L in lens_new) + 4
+    kp = torch.randn(NB, H, bs, D, generator=gen).to(dtype).to(device)
+    vp = torch.randn(NB, H, bs, D, generator=gen).to(dtype).to(device)
+    tables = random_tables(rng, lens_new, NB, bs)
+    width = max(max(len(t) for t in tables), 1) + 1
+    table = np.full((B, width), -1, dtype=np.int32)
+    for b, t in enumerate(tables):
+        table[b, :len(t)] = t
+    x = torch.randn(B, T, 3, H, D, generator=gen).to(dtype).to(device)
+    q, k_new, v_new = (x[:, :, i].transpose(1, 2) for i in range(3))
+    return dict(B=B, H=H, D=D, bs=bs, T=T, dtype=dtype, kp=kp, vp=vp, tables=tables,
+                table=torch.from_numpy(table).to(device), width=width, q=q, k_new=k_new, v_new=v_new,
+                starts=list(prefixes), app=list(app), lens_new=lens_new, NB=NB)
+
+
+def _prefill_ws(pr, device):
+    n = _lib.load().b2pa_paged_prefill_workspace_size(pr["B"], pr["H"], pr["T"], pr["D"], pr["width"], pr["bs"],
+                                                      _lib.dtype_code(pr["dtype"]))
+    return torch.empty(max(n, 1) + 256, dtype=torch.uint8, device=device)
+
+
+def _prefill_unfused(pr, device):
+    lib = _lib.load()
+    kp, vp = pr["kp"].clone(), pr["vp"].clone()
+    st, sh, dt = _lib.status_buffer(device).data_ptr(), _lib.stream_handle(device), _lib.dtype_code(pr["dtype"])
+    starts, lens, seq = _i32(pr["starts"], device), _i32(pr["app"], device), _i32(pr["lens_new"], device)
+    _lib.check(lib.b2pa_kv_append(pr["k_new"].data_ptr(), _lib.strides4(pr["k_new"]), pr["v_new"].data_ptr(),
+                                  _lib.strides4(pr["v_new"]), kp.data_ptr(), vp.data_ptr(), _lib.strides4(kp),
+                                  pr["NB"], pr["table"].data_ptr(), pr["width"], pr["width"], starts.data_ptr(),
+                                  lens.data_ptr(), pr["B"], pr["H"], pr["T"], pr["D"], pr["bs"], dt, st, sh),
+               "append")
+    out = torch.empty_like(pr["q"])
+    ws = _prefill_ws(pr, device)
+    _lib.check(lib.b2pa_paged_prefill(pr["q"].data_ptr(), _lib.strides4(pr["q"]), kp.data_ptr(), vp.data_ptr(),
+                                      _lib.strides4(kp), pr["NB"], pr["table"].data_ptr(), pr["width"], pr["width"],
+                                      seq.data_ptr(), lens.data_ptr(), out.data_ptr(), _lib.strides4(out), pr["B"],
+                                      pr["H"], pr["T"], pr["D"], pr["bs"], 1.0 / math.sqrt(pr["D"]), dt,
+                                      ws.data_ptr(), ws.numel(), st, sh), "prefill")
+    torch.cuda.synchronize()
+    return out, kp, vp
+
+
+def _prefill_fused(pr, device, starts=None):
+    lib = _lib.load()
+    kp, vp = pr["kp"].clone(), pr["vp"].clone()
+    starts = _i32(pr["starts"] if starts is None else starts, device)
+    lens, seq = _i32(pr["app"], device), _i32(pr["lens_new"], device)
+    seq_out = torch.full((pr["B"],), -7, dtype=torch.int64, device=device)
+    out = torch.empty_like(pr["q"])
+    ws = _prefill_ws(pr, device)
+    rc = lib.b2pa_paged_prefill_append(
+        pr["q"].data_ptr(), _lib.strides4(pr["q"]), pr["k_new"].data_ptr(), _lib.strides4(pr["k_new"]),
+        pr["v_new"].data_ptr(), _lib.strides4(pr["v_new"]), kp.data_ptr(), vp.data_ptr(), _lib.strides4(kp),
+        pr["NB"], pr["table"].data_ptr(), pr["width"], pr["width"], seq.data_ptr(), lens.data_ptr(),
+        starts.data_ptr(), lens.data_ptr(), seq_out.data_ptr(), out.data_ptr(), _lib.strides4(out), pr["B"],
+        pr["H"], pr["T"], pr["D"], pr["bs"], 1.0 / math.sqrt(pr["D"]), _lib.dtype_code(pr["dtype"]),
+        ws.data_ptr(), ws.numel(), _lib.status_buffer(device).data_ptr(), _lib.stream_handle(device))
+    _lib.check(rc, "b2pa_paged_prefill_append")
+    torch.cuda.synchronize()
+    return out, kp, vp, seq_out
+
+
+@pytest.mark.parametrize("dtype,D,bs", [(torch.float32, 64, 16), (torch.float32, 64, 8), (torch.float32, 64, 32),
+                                        (torch.float32, 128, 16), (torch.bfloat16, 64, 16),
+                                        (torch.float16, 128, 32)])
+def test_prefill_append_equals_append_then_prefill(cuda_device, dtype, D, bs):
+    """b2pa_paged_prefill_append (fp32 head_dim 64: the append inside the
+    tensor-core path's page copy; otherwise append kernel + prefill) leaves
+    the same pool bytes and output as b2pa_kv_append + b2pa_paged_prefill:
+    prefixes across page boundaries, a padded chunk, an empty sequence
+    growing, a sequence without new tokens."""
+    pr = _prefill_problem(cuda_device, H=3, D=D, bs=bs, T=40, dtype=dtype, prefixes=[0, 13, 70, 16, 5],
+                          app=[40, 25, 40, 1, 0], seed=D + bs)
+    b2pa.clear_status(cuda_device)
+    out_a, kp_a, vp_a = _prefill_unfused(pr, cuda_device)
+    out_b, kp_b, vp_b, seq_out = _prefill_fused(pr, cuda_device)
+    assert b2pa.read_status(cuda_device) == 0
+    assert np.array_equal(_bits(kp_a), _bits(kp_b))
+    assert np.array_equal(_bits(vp_a), _bits(vp_b))
+    assert np.array_equal(_bits(out_a), _bits(out_b))
+    assert seq_out.tolist() == pr["lens_new"]
+    ref = orc.paged_attention_c(pr["q"].float().cpu().numpy(), kp_b.float().cpu().numpy(),
+                                vp_b.float().cpu().numpy(), pr["tables"], pr["lens_new"], pr["app"])
+    np.testing.assert_allclose(out_b.float().cpu().numpy(), ref, **TOL[dtype])
+
+
+def test_prefill_append_refuses_a_chunk_that_does_not_end_the_sequence(cuda_device):
+    pr = _prefill_problem(cuda_device, H=2, D=64, bs=16, T=20, dtype=torch.float32, prefixes=[30, 10],
+                          app=[20, 20], seed=4)
+    b2pa.clear_status(cuda_device)
+    _, kp, vp, _ = _prefill_fused(pr, cuda_device, starts=[30, 3])  # row 1 claims positions 3..22
+    assert b2pa.read_status(cuda_device) == _lib.STATUS_CODES["B2PA_ERR_INVALID_ARGUMENT"]
+    b2pa.clear_status(cuda_device)
+    for blk in pr["tables"][1]:  # sequence 1 was not written
+        assert torch.equal(kp[blk], pr["kp"][blk]) and torch.equal(vp[blk], pr["vp"][blk])
+    assert torch.equal(kp[pr["tables"][0][2], :, 0], pr["k_new"][0, :, 2])  # position 32 of sequence 0 was
