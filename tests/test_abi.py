@@ -109,6 +109,24 @@ def test_decode_append_argument_validation(lib):
     assert _decode_append(lib, B=0) == 0                             # empty batch: nothing to do
 
 
+def test_prefill_append_argument_validation(lib):
+    """b2pa_paged_prefill_append rejects bad arguments before launching."""
+    i64 = lambda t: (ctypes.c_int64 * 4)(*t)
+    B, H, T, D, bs, mp = 1, 1, 8, 64, 16, 4
+    qs = (T * H * D, D, H * D, 1)
+
+    def call(kn=8192, ks=qs, st=8, T=T, dt=0):
+        return lib.b2pa_paged_prefill_append(4096, i64(qs), kn, i64(ks), 12288, i64(qs), 16, 16,
+                                             i64((H * bs * D, bs * D, D, 1)), 10, 8, mp, mp, 8, 8, st, 8, None,
+                                             8192, i64(qs), B, H, T, D, bs, 0.125, dt, 256, 1 << 30, None, None)
+
+    assert call(kn=0) == -1                      # null k_new
+    assert call(st=0) == -1                      # null start positions
+    assert call(ks=(T * H * D, D, H * D, 2)) == -2  # non-unit head_dim stride
+    assert call(dt=7) == -2
+    assert call(T=0) == 0                        # empty chunk: nothing to do
+
+
 def test_prefill_f32_split_needs_its_workspace(lib):
     """fp32 head_dim 64 prefill runs on split copies of the pages held in the
     workspace: a missing or short workspace is refused before any launch."""
