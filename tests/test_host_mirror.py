@@ -237,3 +237,66 @@ def test_deferred_append_is_flushed_before_pool_changes(monkeypatch):
     finally:
         b2pa.set_fused_append(prev)
     assert b2pa.set_fused_append(prev) == prev
+
+
+def test_install_into_reference_rebinds_and_restores(tmp_path, monkeypatch):
+    """install_into_reference on a stand-in package laid out like the
+    reference (src/kernels/paged_attention.py, src/model/attention.py binding
+    paged_attention by name, src/cache/paged_kv.py): all three call sites are
+    rebound, CPU tensors and "paged_reference" still take the reference's own
+    functions, an unknown backend is refused like the reference does,
+    ``fuse_append`` switches the deferred append on, and uninstall() restores
+    every original and the previous switch."""
+    import importlib
+    from types import SimpleNamespace
+
+    from b2pa import paged_kv as pk
+
+    pkg = tmp_path / "fakeref"
+    files = {
+        "__init__.py": "",
+        "kernels/__init__.py": "from .paged_attention import paged_attention\n",
+        "kernels/paged_attention.py": ("CALLS = []\n"
+                                       "def paged_attention(backend, q, kv_cache, current_lengths):\n"
+                                       "    CALLS.append(backend)\n"
+                                       "    return 'reference attention'\n"),
+        "model/__init__.py": "",
+        "model/attention.py": "from fakeref.kernels.paged_attention import paged_attention\n",
+        "cache/__init__.py": "",
+        "cache/paged_kv.py": ("class BatchedPagedKVCache:\n"
+                              "    def append_batch(self, k_new, v_new, current_lengths=None):\n"
+                              "        return 'reference append'\n"),
+    }
+    for name, text in files.items():
+        (pkg / name).parent.mkdir(parents=True, exist_ok=True)
+        (pkg / name).write_text(text)
+    monkeypatch.syspath_prepend(str(tmp_path))
+    km = importlib.import_module("fakeref.kernels.paged_attention")
+    mm = importlib.import_module("fakeref.model.attention")
+    cm = importlib.import_module("fakeref.cache.paged_kv")
+    kpkg = importlib.import_module("fakeref.kernels")
+    orig_pa, orig_append = km.paged_attention, cm.BatchedPagedKVCache.append_batch
+
+    prev = b2pa.set_fused_append(False)
+    try:
+        handle = b2pa.install_into_reference("fakeref", fuse_append=True)
+        try:
+            assert km.paged_attention is mm.paged_attention is kpkg.paged_attention
+            assert km.paged_attention is not orig_pa
+            assert cm.BatchedPagedKVCache.append_batch is not orig_append
+            assert pk._fused_append is True
+            cpu_q = torch.zeros(1, 1, 1, 4)
+            assert mm.paged_attention("triton_paged", cpu_q, None, 1) == "reference attention"
+            assert mm.paged_attention("paged_reference", SimpleNamespace(is_cuda=True), None, 1) == \
+                "reference attention"
+            assert km.CALLS == ["triton_paged", "paged_reference"]
+            with pytest.raises(ValueError, match="Unsupported"):
+                mm.paged_attention("nope", SimpleNamespace(is_cuda=True), None, 1)
+            assert cm.BatchedPagedKVCache().append_batch(cpu_q, cpu_q, 1) == "reference append"
+        finally:
+            handle.uninstall()
+        assert km.paged_attention is orig_pa and mm.paged_attention is orig_pa and kpkg.paged_attention is orig_pa
+        assert cm.BatchedPagedKVCache.append_batch is orig_append
+        assert pk._fused_append is False
+    finally:
+        b2pa.set_fused_append(prev)
