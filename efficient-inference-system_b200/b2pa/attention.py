@@ -121,7 +121,7 @@ def paged_attention(backend: str, q: torch.Tensor, kv_cache, current_lengths) ->
         flush_pending(pool)
     if pool.k_blocks is None:
         # Nothing was ever appended to this layer: every row sees no key, which
-        # the reference defines as a zero output (reference_paged_attention.py:67,102).
+        # the reference defines as a zero output (reference_paged_attention.py:16,51-52).
         return torch.zeros_like(q)
     if host_cur is not None:
         page_table, seq_lens, cur, max_pages = block_table_and_lengths(kv_cache, dev, [host_cur], transient=True)
@@ -207,8 +207,10 @@ def _prefill_with_append(q, kv_cache, current_lengths, host_cur, pend) -> torch.
         ws.data_ptr() if ws is not None else None, ws.numel() if ws is not None else 0,
         _lib.status_buffer(dev).data_ptr(), _lib.stream_handle(dev))
     if rc != 0:
-        # Nothing was launched: append with the ordinary kernel so the pool
-        # ends as the reference's append leaves it, then report.
+        # The attention did not run.  On the non-fused path the append kernel
+        # may already have been queued; appending again with the ordinary
+        # kernel writes the same bytes, and leaves the pool as the
+        # reference's append does either way.  Then report.
         err = _lib.last_error()
         seq = _kv_append(kv_cache, k_new, v_new, pend.starts, pend.lengths)
         pend.seq_out.copy_(seq)

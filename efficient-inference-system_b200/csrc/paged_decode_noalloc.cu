@@ -22,10 +22,14 @@
 //     kernels overlap on the GPU (different streams, no ordering between
 //     them) race on the array and produce garbage; order such calls on one
 //     stream or with events.
-//   * the first call on each device looks up the array's device address with
-//     cudaGetSymbolAddress, which makes the CUDA runtime load this module on
-//     that device.  Make that first call outside any stream capture (a warm-up
-//     call at start-up is enough); later calls only read the cached address.
+//   * the first call in each CUDA context looks up the array's device address
+//     with cudaGetSymbolAddress, which makes the CUDA runtime load this module
+//     on that device.  Make that first call outside any stream capture (a
+//     warm-up call at start-up is enough); a first call on a capturing stream
+//     returns B2PA_ERR_UNSUPPORTED.  Later calls in the same context read the
+//     cached address; a new context on the device (cudaDeviceReset, or the
+//     primary context released and created again) counts as a first call.
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -45,25 +49,78 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
-void* g_addr[kMaxDevices] = {nullptr};
+// Per device: the array's address and the id of the context it was looked up
+// in.  A context created anew on that device (after cudaDeviceReset, or after
+// the primary context was released and retained again) has another id, so the
+// address is looked up again instead of reusing one that no longer exists.
+struct CachedAddress {
+  unsigned long long ctx_id;
+  void* addr;
+};
+CachedAddress g_addr[kMaxDevices] = {};
 
-// Device address of g_noalloc_scratch on the current device; looked up once
-// per device with that device current.
-int scratch_address(void** out) {
+using CtxGetCurrentFn = CUresult (*)(CUcontext*);
+using CtxGetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+
+template <typename Fn>
+Fn driver_fn(const char* name) {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint(name, &p, cudaEnableDefault, &q) == cudaSuccess && q == cudaDriverEntryPointSuccess)
+    return reinterpret_cast<Fn>(p);
+  return nullptr;
+}
+
+// Identifies the current context: its process-unique id (cuCtxGetId), or its
+// handle where the driver lacks that call.
+int current_context_id(unsigned long long* id) {
+  static std::once_flag once;
+  static CtxGetCurrentFn get_current = nullptr;
+  static CtxGetIdFn get_id = nullptr;
+  std::call_once(once, [] {
+    get_current = driver_fn<CtxGetCurrentFn>("cuCtxGetCurrent");
+    get_id = driver_fn<CtxGetIdFn>("cuCtxGetId");
+  });
+  if (get_current == nullptr)
+    return set_error(B2PA_ERR_CUDA, "paged_decode_noalloc: the driver has no cuCtxGetCurrent");
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr)
+    return set_error(B2PA_ERR_CUDA, "paged_decode_noalloc: no current CUDA context");
+  unsigned long long v = 0;
+  if (get_id == nullptr || get_id(ctx, &v) != CUDA_SUCCESS) v = (unsigned long long)(uintptr_t)ctx;
+  *id = v;
+  return B2PA_OK;
+}
+
+// Device address of g_noalloc_scratch in the current context; looked up once
+// per context with its device current.  The look-up may load this module on
+// the device, which must not happen inside a stream capture: a first call
+// that finds `stream` capturing is refused.
+int scratch_address(cudaStream_t stream, void** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_decode_noalloc: cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices)
     return set_error(B2PA_ERR_UNSUPPORTED, "paged_decode_noalloc: device %d out of range", dev);
+  unsigned long long ctx_id = 0;
+  const int rc = current_context_id(&ctx_id);
+  if (rc != B2PA_OK) return rc;
   std::lock_guard<std::mutex> g(g_mu);
-  if (g_addr[dev] == nullptr) {
+  if (g_addr[dev].addr == nullptr || g_addr[dev].ctx_id != ctx_id) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    e = cudaStreamIsCapturing(stream, &cap);
+    if (e != cudaSuccess || cap != cudaStreamCaptureStatusNone)
+      return set_error(B2PA_ERR_UNSUPPORTED,
+                       "paged_decode_noalloc: the first call in a CUDA context looks up the scratch array and "
+                       "cannot run inside a stream capture; make one call before capturing");
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || p == nullptr)
       return set_error(B2PA_ERR_CUDA, "paged_decode_noalloc: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    g_addr[dev] = p;
+    g_addr[dev].addr = p;
+    g_addr[dev].ctx_id = ctx_id;
   }
-  *out = g_addr[dev];
+  *out = g_addr[dev].addr;
   return B2PA_OK;
 }
 
@@ -88,7 +145,7 @@ extern "C" int b2pa_paged_decode_noalloc(const void* q, const int64_t q_strides[
   }
   void* scratch = nullptr;
   if (B > 0) {
-    const int rc = scratch_address(&scratch);
+    const int rc = scratch_address(static_cast<cudaStream_t>(stream), &scratch);
     if (rc != B2PA_OK) return rc;
   }
   return b2pa_paged_decode(q, q_strides, k_pool, v_pool, pool_strides, num_blocks, page_table, pt_stride, max_pages,

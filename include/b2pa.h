@@ -179,8 +179,10 @@ B2PA_API int b2pa_paged_decode_append(const void* q, const int64_t q_strides[4],
  * loads it until exit.  Problems whose b2pa_paged_decode_workspace_size()
  * exceeds that return B2PA_ERR_WORKSPACE.  All calls on a device share the
  * array: calls that may overlap on the GPU (unordered streams) race.  The
- * first call on each device looks the array up (cudaGetSymbolAddress), so
- * make it before any stream capture.  Allocates nothing.
+ * first call in each CUDA context looks the array up (cudaGetSymbolAddress),
+ * so make it before any stream capture: a first call on a capturing stream
+ * returns B2PA_ERR_UNSUPPORTED.  A context created anew on the device (after
+ * cudaDeviceReset) looks the array up again.  Allocates nothing.
  */
 #define B2PA_NOALLOC_SCRATCH_BYTES (32u << 20)
 B2PA_API int b2pa_paged_decode_noalloc(const void* q, const int64_t q_strides[4],
@@ -237,9 +239,13 @@ B2PA_API int b2pa_paged_prefill(const void* q, const int64_t q_strides[4],
  * seq_lens_out (may be NULL) receives seq_lens as int64, the value
  * append_batch returns.  For fp32 pools with head_dim 64 the append happens
  * inside the launch that copies the pages for the tensor cores; otherwise
- * the append kernel runs first.  Same workspace as b2pa_paged_prefill.  Pool
- * bytes and outputs are identical to b2pa_kv_append followed by
- * b2pa_paged_prefill.
+ * the append kernel runs first.  Same workspace as b2pa_paged_prefill.  For
+ * inputs that meet the contract above (start_pos[b] + min(lengths[b], T) ==
+ * seq_lens[b], every page a row lands on present in the table) pool bytes and
+ * outputs are identical to b2pa_kv_append followed by b2pa_paged_prefill.
+ * Inputs that break it are handled differently by the two paths: the fused
+ * fp32 path skips the offending rows and sets the status word, the others
+ * append them as b2pa_kv_append would.
  */
 B2PA_API int b2pa_paged_prefill_append(const void* q, const int64_t q_strides[4],
                        const void* k_new, const int64_t new_k_strides[4],

@@ -37,12 +37,12 @@ LIB_PATH = ORACLE_DIR / "liboracle.so"
 # ------------------------------------------------------------------ attention
 def visible_count(seq_len: int, cur_len: int, t: int) -> int:
     """Keys row t sees: tokens j < seq_len with j <= seq_len - cur_len + t
-    (reference_paged_attention.py:84-93)."""
+    (reference_paged_attention.py:36,40-42)."""
     return max(0, min(seq_len, seq_len - cur_len + t + 1))
 
 
 def gather_tokens(pool: np.ndarray, block_ids, h: int, n: int) -> np.ndarray:
-    """Rows 0..n-1 of head h through the block table (reference_paged_attention.py:95-98)."""
+    """Rows 0..n-1 of head h through the block table (reference_paged_attention.py:44-47)."""
     bs = pool.shape[2]
     if n == 0:
         return np.zeros((0, pool.shape[3]), dtype=pool.dtype)

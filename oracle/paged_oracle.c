@@ -8,15 +8,15 @@
  * the timed CPU baseline.  Nothing in the b2pa package links or calls it.
  *
  * Algorithm, per (sequence b, head h, query row t), exactly as the reference
- * loops (reference_paged_attention.py:82-108):
- *   past = seq_len[b] - cur_len[b]                       (:83-84)
- *   pos  = past + t                                      (:87)
- *   for token j = 0 .. seq_len-1, stopping at j > pos:   (:91-93)
- *       block = block_ids[j / block_size], off = j % block_size   (:95-96)
- *       score_j = dot(q[b,h,t,:], K[block,h,off,:]) * scale        (:99)
- *   no token -> output row stays 0                       (:67, :102-103)
- *   w = softmax(score) (max-subtracted, as torch.softmax) (:106)
- *   out[b,h,t,:] = sum_j w_j * V[block,h,off,:]          (:107-108)
+ * loops (reference_paged_attention.py:31-57):
+ *   past = seq_len[b] - cur_len[b]                       (:32-33)
+ *   pos  = past + t                                      (:36)
+ *   for token j = 0 .. seq_len-1, stopping at j > pos:   (:40-42)
+ *       block = block_ids[j / block_size], off = j % block_size   (:44-45)
+ *       score_j = dot(q[b,h,t,:], K[block,h,off,:]) * scale        (:46-48)
+ *   no token -> output row stays 0                       (:16, :51-52)
+ *   w = softmax(score) (max-subtracted, as torch.softmax) (:54-55)
+ *   out[b,h,t,:] = sum_j w_j * V[block,h,off,:]          (:56-57)
  * in float32, like the reference's float32 tensors.  Rows are independent;
  * they are spread over `nthreads` POSIX threads (0 = all online CPUs).
  *
@@ -47,7 +47,7 @@ typedef struct {
   atomic_int bad;
 } Job;
 
-/* One (b, h, t) row of reference_paged_attention.py:86-108. */
+/* One (b, h, t) row of reference_paged_attention.py:35-57. */
 static void attend_row(Job* j, int64_t r, float* sc) {
   const int H = j->H, T = j->T, D = j->D, BS = j->BS;
   const int b = (int)(r / ((int64_t)H * T));

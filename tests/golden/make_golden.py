@@ -228,12 +228,12 @@ CASES = {
     "model_config0": lambda ref: _model_case(REF_PATH[0], tiny=False),
     "serving_config3": lambda ref: _serving_case(),
 }
-REF_PATH = ["/root/reference"]
+REF_PATH = [None]  # the reference checkout, from --reference
 
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of a checkout of the reference repository")
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
     torch.set_num_threads(1)

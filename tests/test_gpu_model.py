@@ -16,7 +16,6 @@ reference's attention on the same GPU.
 from __future__ import annotations
 
 import json
-import os
 import time
 
 import numpy as np
@@ -115,9 +114,6 @@ def test_config0_end_to_end(cuda_device, fused):
               "b2pa_seconds": secs_b, "b2pa_tokens_per_s": 128 / secs_b,
               "torch_reference_on_gpu_seconds": secs_r}
     print(json.dumps(report))
-    if os.path.isdir("gpurun_out"):
-        with open(f"gpurun_out/e2e_config0{'_fused' if fused else ''}.json", "w") as f:
-            json.dump(report, f)
 
 
 @pytest.mark.parametrize("fused", [False, True], ids=["append_then_decode", "fused_append"])

@@ -9,7 +9,6 @@ measured GPU time as in the reference."""
 from __future__ import annotations
 
 import json
-import os
 import time
 
 import numpy as np
@@ -97,6 +96,3 @@ def test_config3_serving_trace(cuda_device):
             "virtual_gpu_ms": sum(e[3] for e in events), "wall_s": wall,
         }
     print(json.dumps(report))
-    if os.path.isdir("gpurun_out"):
-        with open("gpurun_out/serving_config3.json", "w") as f:
-            json.dump(report, f)
