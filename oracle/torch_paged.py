@@ -12,7 +12,11 @@ projections, different attention path):
 * ``paged_attention_torch`` restates paged_attention_reference
   (src/kernels/reference_paged_attention.py:10-59), vectorised per sequence:
   scores = q.K^T * scale, keys visible iff key <= seq_len - cur_len + t and
-  key < seq_len, softmax, weighted sum; rows with no key are zero.
+  key < seq_len, softmax, weighted sum; rows with no key are zero;
+* ``paged_attention_token_loop`` restates the same function with the
+  reference's own loop structure (one ``torch.dot`` per visible token and
+  head), so that bench.py can time the reference's CPU path per
+  (token, head) without the reference installed.
 """
 from __future__ import annotations
 
@@ -148,4 +152,36 @@ def paged_attention_torch(q: torch.Tensor, kv_cache, current_lengths) -> torch.T
         w = torch.softmax(s, dim=-1)
         w = torch.where(any_vis.view(1, T, 1), w, torch.zeros_like(w))
         out[b] = torch.matmul(w, V)
+    return out
+
+
+def paged_attention_token_loop(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor, block_ids: list[int],
+                               seq_len: int, cur_len: int, heads=None) -> torch.Tensor:
+    """The reference's CPU attention path with its cost structure kept: one
+    sequence, a Python loop over (head, query row, visible token) with one
+    pool row read for K and one for V and a ``torch.dot`` per token, then
+    ``torch.stack`` / ``torch.softmax`` / weighted sum per row
+    (reference_paged_attention.py:31-57).  ``paged_attention_torch`` above is
+    the same math vectorised; this form exists to time what the reference's
+    own loop costs per (token, head) on a CPU.  q: [H, T, D]; returns
+    [len(heads), T, D] for the heads given (default all)."""
+    H, T, D = q.shape
+    bs = k_pool.shape[2]
+    scale = 1.0 / math.sqrt(D)
+    heads = range(H) if heads is None else heads
+    out = torch.zeros(len(heads), T, D, dtype=q.dtype)
+    first_query_pos = seq_len - cur_len
+    for oh, h in enumerate(heads):
+        for t in range(T):
+            last = min(seq_len - 1, first_query_pos + t)
+            if last < 0:
+                continue
+            scores, values = [], []
+            qv = q[h, t]
+            for j in range(last + 1):
+                blk, off = block_ids[j // bs], j % bs
+                scores.append(torch.dot(qv, k_pool[blk, h, off, :]) * scale)
+                values.append(v_pool[blk, h, off, :])
+            w = torch.softmax(torch.stack(scores), dim=0)
+            out[oh, t] = torch.sum(w.unsqueeze(-1) * torch.stack(values, dim=0), dim=0)
     return out

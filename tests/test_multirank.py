@@ -1,6 +1,7 @@
 """Host-side logic of the multi-GPU bench path on CPU with the gloo backend
 (world size 2): every sequence is owned by exactly one rank, weak scaling
-gives each rank the same count, and timings reduce to the max over ranks."""
+gives each rank the same count, timings reduce to the max over ranks, and
+the launch parity check reduces to the worst rank."""
 from __future__ import annotations
 
 import os
@@ -39,6 +40,12 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         t = bench.max_over_ranks([1.0 + rank, 5.0 - rank], torch.device("cpu"), world)
         if rank == 0:
             np.save(os.path.join(out_dir, "max.npy"), np.array(t))
+        # parity of the benchmarked launch: worst case over ranks (rank 1's rows differ)
+        mine = {"seqs": 5, "max_abs_err": 0.01 * (rank + 1), "tolerance": "t", "outputs_ok": True,
+                "appended_rows_checked": 10 + rank, "appended_rows_bit_exact": rank == 0, "ok": rank == 0}
+        red = bench.reduce_parity(torch, mine, torch.device("cpu"), world)
+        if rank == 0:
+            np.save(os.path.join(out_dir, "parity.npy"), np.array([red], dtype=object), allow_pickle=True)
     finally:
         dist.destroy_process_group()
 
@@ -57,6 +64,10 @@ def test_partition_and_max_reduction(tmp_path):
     assert len(weak[0]) == len(weak[1]) == 37           # weak: 37 per rank
     assert sorted(x for p in weak for x in p) == sorted(bench.all_lengths(74).tolist())
     assert np.load(tmp_path / "max.npy").tolist() == [2.0, 5.0]
+    red = np.load(tmp_path / "parity.npy", allow_pickle=True)[0]
+    assert red["seqs"] == 10 and red["ranks"] == 2 and red["appended_rows_checked"] == 21
+    assert abs(red["max_abs_err"] - 0.02) < 1e-12
+    assert red["ok"] is False and red["appended_rows_bit_exact"] is False
 
 
 def _failing_worker(rank: int, world: int, port: int, out_dir: str, mode: str) -> None:

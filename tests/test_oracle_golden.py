@@ -85,3 +85,22 @@ def test_visible_count_rules():
     assert orc.visible_count(20, 5, 0) == 16
     assert orc.visible_count(0, 0, 0) == 0
     assert orc.visible_count(3, 5, 0) == 0
+
+
+@pytest.mark.parametrize("name", ["decode_f32_curvar", "prefill_f32_bs8_d16", "decode_bf16_bs16_d128"])
+def test_token_loop_restatement_matches_reference(name):
+    """The per-token loop form bench.py times as the reference's CPU path
+    computes the reference's outputs."""
+    import torch
+
+    from oracle import torch_paged as tp
+
+    g = load_golden(name)
+    dt = str(g["dtype"])
+    q, kp, vp = _f32(g["q"], dt), _f32(g["k_pool"], dt), _f32(g["v_pool"], dt)
+    tables = split_tables(g["block_ids"], g["block_counts"])
+    kt, vt = torch.from_numpy(kp), torch.from_numpy(vp)
+    for b in range(q.shape[0]):
+        out = tp.paged_attention_token_loop(torch.from_numpy(q[b]), kt, vt, tables[b], int(g["seq_lens"][b]),
+                                            int(g["cur_lens"][b]))
+        np.testing.assert_allclose(out.numpy(), g["out"][b], rtol=2e-5, atol=2e-6)
