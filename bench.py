@@ -531,7 +531,8 @@ def e2e_leg(torch, b2pa, wl: Workload, dev, lens_now: np.ndarray, warmup: int, s
     q (one fused-QKV pinned buffer) and copies its output back to pinned host
     memory, whose arrival the host waits for.  The copies are pipelined as a
     serving loop would: step i+1's upload runs on a copy stream into a second
-    device buffer while step i decodes, and the host waits for step i's
+    device buffer while step i decodes, step i's output goes down on another
+    copy stream while step i+1 decodes, and the host waits for step i's
     output after it has launched step i+1.  Returns device ms for ``steps``."""
     import torch.distributed as dist
 
@@ -539,6 +540,7 @@ def e2e_leg(torch, b2pa, wl: Workload, dev, lens_now: np.ndarray, warmup: int, s
     B = wl.B
     comp = torch.cuda.current_stream(dev)
     copy_stream = torch.cuda.Stream(dev)
+    d2h_stream = torch.cuda.Stream(dev)
     host_kvq = torch.randn(B, 1, 3, H, D, dtype=torch.bfloat16).pin_memory()
     host_out = [torch.empty(B, H, 1, D, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
     dev_kvq = [torch.empty(B, 1, 3, H, D, dtype=torch.bfloat16, device=dev) for _ in range(2)]
@@ -561,9 +563,12 @@ def e2e_leg(torch, b2pa, wl: Workload, dev, lens_now: np.ndarray, warmup: int, s
         k, v, q = (dev_kvq[j][:, :, c].transpose(1, 2) for c in range(3))
         cache.append_batch(k, v, 1)
         out = b2pa.paged_attention("b200_paged", q, cache, 1)
-        free_ev[j].record(comp)
-        host_out[j].copy_(out, non_blocking=True)
-        out_ev[j].record(comp)
+        free_ev[j].record(comp)                     # also: this step's output is written
+        d2h_stream.wait_event(free_ev[j])
+        out.record_stream(d2h_stream)
+        with torch.cuda.stream(d2h_stream):
+            host_out[j].copy_(out, non_blocking=True)
+        out_ev[j].record(d2h_stream)
 
     def run(n):
         copy_stream.wait_stream(comp)
@@ -585,6 +590,7 @@ def e2e_leg(torch, b2pa, wl: Workload, dev, lens_now: np.ndarray, warmup: int, s
         e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e_start.record(comp)
         run(steps)
+        comp.wait_stream(d2h_stream)
         e_end.record(comp)
         torch.cuda.synchronize(dev)
     finally:
@@ -733,7 +739,8 @@ def main(argv=None) -> int:
             "h2d_bytes_per_step": 3 * B * H * D * 2,
             "d2h_bytes_per_step": B * H * D * 2,
             "path": "b2pa.BatchedPagedKVCache.append_batch + b2pa.paged_attention, pinned host inputs and outputs, "
-                    "uploads on a copy stream one step ahead, output awaited after the next step's launch"
+                    "uploads on a copy stream one step ahead, outputs down on another copy stream and awaited "
+                    "after the next step's launch"
                     + (", b2pa.set_fused_append(True)" if fused else ""),
         },
         "strong": strong,
