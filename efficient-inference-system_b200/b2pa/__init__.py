@@ -15,6 +15,7 @@ from .attention import (
     paged_attention_prefill_b200,
 )
 from .integration import install_into_reference
+from .serving import ContinuousBatchingRank, LeastOutstandingTokensRouter, ServeResult, gather_request_times, serve
 from .paged_kv import (
     BatchedPagedKVCache,
     LayerBlockPool,
@@ -26,6 +27,11 @@ from .paged_kv import (
 
 __all__ = [
     "BatchedPagedKVCache",
+    "ContinuousBatchingRank",
+    "LeastOutstandingTokensRouter",
+    "ServeResult",
+    "gather_request_times",
+    "serve",
     "LayerBlockPool",
     "PagedKVCacheState",
     "SUPPORTED_BACKENDS",
