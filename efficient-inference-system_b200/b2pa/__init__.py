@@ -15,6 +15,7 @@ from .attention import (
     paged_attention_prefill_b200,
 )
 from .integration import install_into_reference
+from .step import DecodeGraph, DecodeStep, SharedStepMetadata
 from .serving import ContinuousBatchingRank, LeastOutstandingTokensRouter, ServeResult, gather_request_times, serve
 from .paged_kv import (
     BatchedPagedKVCache,
@@ -28,6 +29,9 @@ from .paged_kv import (
 __all__ = [
     "BatchedPagedKVCache",
     "ContinuousBatchingRank",
+    "DecodeGraph",
+    "DecodeStep",
+    "SharedStepMetadata",
     "LeastOutstandingTokensRouter",
     "ServeResult",
     "gather_request_times",

@@ -23,6 +23,7 @@ import torch
 from . import _lib
 from ._metadata import block_table_and_lengths
 from .paged_kv import _kv_append, flush_pending, take_pending
+from .step import _StepPending
 
 # "triton_paged" is accepted so that models configured for the reference's GPU
 # backend (src/model/transformer.py:55,117) run unchanged on this one.
@@ -112,6 +113,13 @@ def paged_attention(backend: str, q: torch.Tensor, kv_cache, current_lengths) ->
         host_cur = [int(x) for x in current_lengths]
     pool = kv_cache.pool
     pend = getattr(pool, "_b2pa_pending", None)
+    step = getattr(pool, "_b2pa_step", None)
+    if step is not None:  # an open DecodeStep: its shared metadata, no host work
+        if not isinstance(pend, _StepPending) or pend.step is not step or T != 1:
+            raise RuntimeError("b2pa: inside a DecodeStep, paged_attention must follow its layer's append_batch")
+        step.layer_of(kv_cache)
+        pool._b2pa_pending = None
+        return step.attend(q, kv_cache, pend)
     if pend is not None:
         if (pend.cache is kv_cache and pend.k_new.shape[2] == T and pend.k_new.device == dev
                 and pool.k_blocks.dtype == q.dtype):

@@ -316,6 +316,9 @@ def plan_append(cache, k_new: torch.Tensor, lengths, as_array: bool = False):
 def append_batch_into(cache, k_new: torch.Tensor, v_new: torch.Tensor, current_lengths=None) -> torch.Tensor:
     """``BatchedPagedKVCache.append_batch`` (paged_kv.py:151-172): host block
     allocation, then one scatter-kernel launch for every copied token."""
+    step = getattr(cache.pool, "_b2pa_step", None)
+    if step is not None:  # an open DecodeStep planned this append already
+        return step.append(cache, k_new, v_new, current_lengths)
     B, H, T, D = k_new.shape
     if B != len(cache.states):
         raise ValueError(f"k_new has {B} rows for {len(cache.states)} states")
@@ -399,6 +402,9 @@ def take_pending(pool):
 def flush_pending(pool) -> None:
     """Performs the pool's deferred decode append now, with the ordinary
     append kernel, and fills the lengths tensor append_batch returned."""
+    pend = getattr(pool, "_b2pa_pending", None)
+    if pend is not None and not isinstance(pend, _PendingAppend):
+        raise RuntimeError("b2pa: the pool is inside an open DecodeStep whose attention has not run yet")
     pend = take_pending(pool)
     if pend is not None:
         seq_lens = _kv_append(pend.cache, pend.k_new, pend.v_new, pend.starts, pend.lengths)
