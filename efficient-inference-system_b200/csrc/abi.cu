@@ -150,19 +150,18 @@ bool prefill_uses_tensor_cores(int D, int block_size, int dtype, int64_t pool_ro
 }
 
 // Split the key range of the tensor-core prefill (query tiles of 128 rows)
-// when the (query tile, head, sequence) CTAs alone would leave most SMs
-// idle.  The split CTAs must fit in one wave of one CTA per SM of a 148-SM
-// part: measured on config[2], a second wave or a second resident CTA per SM
-// costs more (combine pass, shared SM) than the shorter key walks save.  At
-// least 2 key tiles per CTA.  Sets kt_per_split / nsplit_max and the
-// partials' workspace offsets; returns the partials' bytes.
-static size_t tc_key_split(PrefillPlan& pl, int B, int H, int T, int D, int64_t ktmax) {
+// when the (query tile, head, sequence) CTAs alone would leave SMs idle: the
+// split CTAs fill one wave of `slots` resident CTAs (148 SMs x CTAs per SM),
+// at least 2 key tiles each.  A second wave costs more (combine pass, shared
+// SM) than the shorter key walks save.  Sets kt_per_split / nsplit_max and
+// the partials' workspace offsets; returns the partials' bytes.
+static size_t tc_key_split(PrefillPlan& pl, int B, int H, int T, int D, int64_t ktmax, int64_t slots,
+                           int64_t kt_cap) {
   if (B <= 0 || T <= 0 || ktmax <= 2) return 0;
   const int64_t ctas = (int64_t)B * H * ((T + 127) / 128);
-  int64_t splits = 148 / ctas;
+  int64_t splits = slots / ctas;
   // A CTA stages the block ids of its key range in shared memory: at most
-  // 1024 key tiles (64k keys) per CTA.
-  const int64_t kt_cap = 1024;
+  // kt_cap key tiles per CTA.
   const int64_t min_splits = (ktmax + kt_cap - 1) / kt_cap;
   if (splits < min_splits) splits = min_splits;
   if (splits > ktmax) splits = ktmax;
@@ -173,10 +172,10 @@ static size_t tc_key_split(PrefillPlan& pl, int B, int H, int T, int D, int64_t 
   if (ns <= 1) return 0;
   pl.kt_per_split = (int)kt;
   pl.nsplit_max = (int)ns;
-  const size_t slots = (size_t)B * H * T * ns;
+  const size_t nslots = (size_t)B * H * T * ns;
   pl.off_part_ml = 0;
-  pl.off_part_o = align_up(8 * slots, 256);
-  return align_up(pl.off_part_o + 4 * slots * D, 256);
+  pl.off_part_o = align_up(8 * nslots, 256);
+  return align_up(pl.off_part_o + 4 * nslots * D, 256);
 }
 
 static bool prefill_f32_split_tc(int D, int block_size, int64_t split_rows) {
@@ -190,6 +189,7 @@ static PrefillPlan empty_prefill_plan(int64_t ktmax) {
   pl.kt_per_split = (int)(ktmax > 0 ? ktmax : 1);
   pl.nsplit_max = 1;
   pl.split_tc = 0;
+  pl.pair = 0;
   pl.off_part_ml = pl.off_part_o = pl.off_split_k = pl.off_split_v = pl.off_slots = pl.off_flag = 0;
   pl.bytes = 0;
   return pl;
@@ -224,7 +224,7 @@ PrefillPlan make_prefill_plan(int B, int H, int T, int D, int max_pages, int blo
     // pages (B * max_pages slots of H pages, K and V, 2 * D halves per row),
     // after the partials of its key-range split; then the range flag.
     pl.split_tc = 1;
-    const size_t part = tc_key_split(pl, B, H, T, D, ktmax);
+    const size_t part = tc_key_split(pl, B, H, T, D, ktmax, 148, 1024);
     const size_t slot_bytes = (size_t)H * block_size * 2 * D * 2;
     const size_t nslots = (size_t)B * max_pages;
     pl.off_split_k = align_up(part, 256);
@@ -237,7 +237,10 @@ PrefillPlan make_prefill_plan(int B, int H, int T, int D, int max_pages, int blo
   if (dtype == B2PA_DTYPE_F32 && (D == 64 || D == 128))
     return make_prefill_plan_f32_tiled(B, H, T, D, max_pages, block_size);
   if (!prefill_uses_tensor_cores(D, block_size, dtype, 0)) return pl;
-  pl.bytes = tc_key_split(pl, B, H, T, D, ktmax);
+  // 16-bit head_dim 64: two CTAs per SM (their shared memory allows block
+  // ids of up to 900 key tiles per CTA at that occupancy)
+  pl.pair = D == 64 ? 1 : 0;
+  pl.bytes = pl.pair ? tc_key_split(pl, B, H, T, D, ktmax, 2 * 148, 900) : tc_key_split(pl, B, H, T, D, ktmax, 148, 1024);
   return pl;
 }
 

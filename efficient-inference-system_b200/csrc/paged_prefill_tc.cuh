@@ -112,7 +112,13 @@ __device__ __forceinline__ void prefill_tile_range(const PfTcParams& p, int b, i
 // the general fp32 CUDA-core kernel, launched after this one as a backup that
 // does nothing otherwise.  The K/V pages are split into a workspace copy
 // beforehand (prefill_split_pages_kernel); q and P are split in the kernel.
-template <int D, int BS, bool SPLIT = false>
+// PAIR: the 16-bit head_dim-64 kernel sized to run two CTAs per SM (one
+// softmax warpgroup, 3-stage rings: ~99 KB of shared memory and 256 TMEM
+// columns each), so that a key range split in two keeps every SM busy with
+// two independent tile chains; the per-tile chain (page loads, the Q.K^T /
+// softmax / P.V hand-overs) is latency-bound, so two chains per SM run at
+// nearly twice the rate of one.
+template <int D, int BS, bool SPLIT = false, bool PAIR = false>
 struct PfTcCfg {
   static constexpr int BM = 128;         // query rows per CTA (UMMA M)
   static constexpr int BN = 64;          // keys per tile
@@ -125,12 +131,13 @@ struct PfTcCfg {
   // softmax warps on every SM sub-partition, so one warp's exponentials
   // overlap the other's TMEM loads, barrier waits and P stores.
   // (The fp32 variant, with twice the operand bytes, keeps one group.)
-  static constexpr int NG = !SPLIT && D == 64 ? 2 : 1;
+  static constexpr int NG = !SPLIT && D == 64 && !PAIR ? 2 : 1;
+  static constexpr int CTAS_PER_SM = PAIR ? 2 : 1;
   static constexpr int NSLOT = 2 * NG;  // S/P buffers: two per group
   // Depth of the K ring and of the V ring.  A K stage is refilled once the
   // Q.K^T that read it is done, a V stage once its P.V is done, so each ring
   // loads up to STAGES tiles ahead of its consumer.
-  static constexpr int STAGES = SPLIT ? 3 : (D == 64 ? 6 : 4);
+  static constexpr int STAGES = SPLIT ? 3 : (D == 64 ? (PAIR ? 3 : 6) : 4);
   static constexpr int Q_TILE = BM * D * 2;   // one bf16 / fp16 tile
   static constexpr int KV_TILE = BN * D * 2;
   static constexpr int P_TILE = BM * BN * 2;
@@ -159,6 +166,8 @@ struct PfTcCfg {
   static constexpr int THREADS = SOFTMAX_THREADS + 128;
   static_assert(D == 64 || D == 128, "tcgen05 prefill is built for head_dim 64 and 128");
   static_assert(!SPLIT || D == 64, "the fp32 variant fits shared memory for head_dim 64 only");
+  static_assert(!PAIR || (D == 64 && !SPLIT), "two CTAs per SM: 16-bit head_dim 64 only");
+  static_assert(!PAIR || (SMEM_FIXED <= 100 * 1024 && TMEM_COLS == 256), "two CTAs per SM must fit");
   static_assert(BN % BS == 0 && 32 % PAGES == 0, "block size must divide the key tile");
   static_assert(TMEM_USED <= 512, "TMEM holds 512 columns");
   static_assert(SMEM_FIXED <= 200 * 1024, "shared-memory plan");
@@ -230,12 +239,13 @@ __device__ __forceinline__ void split_f16x8(const float (&f)[8], uint4& hi, uint
   lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-template <typename T, int D, int BS>
-__global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
+template <typename T, int D, int BS, bool PAIR = false>
+__global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>, PAIR>::THREADS,
+                                  PfTcCfg<D, BS, kPfSplit<T>, PAIR>::CTAS_PER_SM)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             PfTcParams p) {
   constexpr bool SPLIT = kPfSplit<T>;
-  using C = PfTcCfg<D, BS, SPLIT>;
+  using C = PfTcCfg<D, BS, SPLIT, PAIR>;
   constexpr int NG = C::NG, NSLOT = C::NSLOT;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
@@ -348,12 +358,12 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
         blk_lane = prefill_checked_block(p, raw, page, kend, BS);
       }
       if (!warp_wait(&empty[st], ph ^ 1u, p.status, abort_flag)) break;
-      int blks[C::PAGES];
+      // lane pg < PAGES issues the loads of page pg of the tile
+      const int my_blk = __shfl_sync(kFullMask, blk_lane, (lp + (lane % C::PAGES)) & 31);
       uint32_t bytes = 0;
 #pragma unroll
       for (int pg = 0; pg < C::PAGES; ++pg) {
         const int blk = __shfl_sync(kFullMask, blk_lane, (lp + pg) & 31);
-        blks[pg] = blk;
         if (blk >= 0) {
           bytes += (uint32_t)(C::NOP * BS * D * 2);
         } else {
@@ -370,22 +380,21 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
       }
       tc::fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&full[st], bytes);
+      // The stage's byte count goes in before any of its loads is issued.
+      if (lane == 0) mbar_arrive_expect_tx(&full[st], bytes);
+      __syncwarp();
+      if (lane < C::PAGES && my_blk >= 0) {
+        const int pg = lane;
+        const int row = (my_blk * p.H + h) * BS;
+        // split variant: the workspace rows hold hi in columns [0, D) and
+        // lo in [D, 2D)
 #pragma unroll
-        for (int pg = 0; pg < C::PAGES; ++pg) {
-          if (blks[pg] < 0) continue;
-          const int row = (blks[pg] * p.H + h) * BS;
-          // split variant: the workspace rows hold hi in columns [0, D) and
-          // lo in [D, 2D)
+        for (int op = 0; op < C::NOP; ++op)
 #pragma unroll
-          for (int op = 0; op < C::NOP; ++op)
-#pragma unroll
-            for (int kb = 0; kb < C::KB; ++kb) {
-              const int off = st * C::KV_BYTES + op * C::KV_TILE + kb * (C::BN * 128) + pg * (BS * 128);
-              tc::tma_load_2d(ring + off, tmap, op * D + kb * 64, row, &full[st]);
-            }
-        }
+          for (int kb = 0; kb < C::KB; ++kb) {
+            const int off = st * C::KV_BYTES + op * C::KV_TILE + kb * (C::BN * 128) + pg * (BS * 128);
+            tc::tma_load_2d(ring + off, tmap, op * D + kb * 64, row, &full[st]);
+          }
       }
       __syncwarp();
     }
@@ -614,29 +623,12 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
       const bool need = mt > m + kRescale;
       const float m_new = need ? mt : m;
       const bool scale_o = need && m != -INFINITY;
-      if (i > 0 && __any_sync(kFullMask, scale_o)) {
-        const float alpha = scale_o ? fast_exp2(m - m_new) : 1.f;
-        // wait for the group's previous P.V before touching its O
-        if (!warp_wait(&o_full[g], (uint32_t)(i - 1) & 1u, p.status, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc::fence_after_sync();
-#pragma unroll
-        for (int cb = 0; cb < D / 32; ++cb) {
-          float ov[32];
-          tc::tmem_ld32(tO + g * D + trow + cb * 32, ov);
-          tc::tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; ++e) ov[e] *= alpha;
-          tc::tmem_st32(tO + g * D + trow + cb * 32, ov);
-        }
-        tc::tmem_wait_st();
-        l *= alpha;
-      }
+      const float alpha = scale_o ? fast_exp2(m - m_new) : 1.f;
       m = m_new;
       // P = 2^(s * sc - m), two lanes per fma; a row with no visible key so
       // far (m = -inf) has every s at -inf, so any finite offset gives 0.
+      // P is written before the (rare) rescale of O below, which frees the
+      // score registers first; P.V cannot start before p_full, after both.
       const float2 sc2 = make_float2(sc, sc);
       const float2 nm2 = make_float2(m == -INFINITY ? 0.f : -m, m == -INFINITY ? 0.f : -m);
       float2 ls[4];  // 8 independent partial sums
@@ -665,7 +657,27 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
         }
       }
       const float2 l01 = add2(ls[0], ls[1]), l23 = add2(ls[2], ls[3]);
-      l += (l01.x + l01.y) + (l23.x + l23.y);
+      const float tile_sum = (l01.x + l01.y) + (l23.x + l23.y);
+      if (i > 0 && __any_sync(kFullMask, scale_o)) {
+        // wait for the group's previous P.V before touching its O
+        if (!warp_wait(&o_full[g], (uint32_t)(i - 1) & 1u, p.status, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after_sync();
+#pragma unroll
+        for (int cb = 0; cb < D / 32; ++cb) {
+          float ov[32];
+          tc::tmem_ld32(tO + g * D + trow + cb * 32, ov);
+          tc::tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) ov[e] *= alpha;
+          tc::tmem_st32(tO + g * D + trow + cb * 32, ov);
+        }
+        tc::tmem_wait_st();
+        l *= alpha;
+      }
+      l += tile_sum;
       tc::fence_proxy_async_smem();
       tc::fence_before_sync();
       __syncwarp();
@@ -699,52 +711,57 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
     }
     constexpr int DC = D / NG;  // columns this thread writes
     const int c0 = g * DC;
-    float o[DC];
+    const bool have_o = ok && ntiles > 0 && warp_wait(o_final, 0u, p.status, abort_flag);  // warp-uniform
+    if (have_o) tc::fence_after_sync();
+    const bool partial = nsplit > 1;
+    const float inv = 1.f / fmaxf(lsum, 1e-9f);
+    const int64_t pslot = (((int64_t)b * p.H + h) * p.T + t) * p.nsplit_max + split;
+    // 32 columns at a time (TMEM loads are warp-collective: every lane runs them)
 #pragma unroll
-    for (int e = 0; e < DC; ++e) o[e] = 0.f;
-    if (ok && ntiles > 0 && warp_wait(o_final, 0u, p.status, abort_flag)) {
-      tc::fence_after_sync();
+    for (int cb = 0; cb < DC / 32; ++cb) {
+      float o[32];
 #pragma unroll
-      for (int gg = 0; gg < NG; ++gg) {
-        if (gg >= ntiles) break;  // group without tiles: its O was never written
+      for (int e = 0; e < 32; ++e) o[e] = 0.f;
+      if (have_o) {
 #pragma unroll
-        for (int cb = 0; cb < DC / 32; ++cb) {
+        for (int gg = 0; gg < NG; ++gg) {
+          if (gg >= ntiles) break;  // group without tiles: its O was never written
           float ov[32];
           tc::tmem_ld32(tO + gg * D + trow + c0 + cb * 32, ov);
           tc::tmem_wait_ld();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[cb * 32 + e] = NG > 1 ? fmaf(wgt[gg], ov[e], o[cb * 32 + e]) : ov[e];
+          for (int e = 0; e < 32; ++e) o[e] = NG > 1 ? fmaf(wgt[gg], ov[e], o[e]) : ov[e];
+        }
+      }
+      if (t >= p.T) continue;
+      if (partial) {
+        float4* po = reinterpret_cast<float4*>(p.part_o + pslot * D + c0 + cb * 32);
+#pragma unroll
+        for (int c4 = 0; c4 < 8; ++c4) po[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
+      } else {
+        T* orow = static_cast<T*>(p.out) + (int64_t)b * p.so_b + (int64_t)h * p.so_h + (int64_t)t * p.so_t + c0 +
+                  cb * 32;
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          float f[8];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) f[e] = o[c8 * 8 + e] * inv;
+          if constexpr (SPLIT) {
+            float4* o4 = reinterpret_cast<float4*>(orow + c8 * 8);
+            o4[0] = make_float4(f[0], f[1], f[2], f[3]);
+            o4[1] = make_float4(f[4], f[5], f[6], f[7]);
+          } else {
+            Vec<T, 8> w;
+            w.from_float(f);
+            *reinterpret_cast<uint4*>(orow + c8 * 8) = w.w;
+          }
         }
       }
     }
     tc::fence_before_sync();
-    if (t < p.T && nsplit > 1) {
-      const int64_t slot = (((int64_t)b * p.H + h) * p.T + t) * p.nsplit_max + split;
-      float4* po = reinterpret_cast<float4*>(p.part_o + slot * D + c0);
-#pragma unroll
-      for (int c4 = 0; c4 < DC / 4; ++c4) po[c4] = make_float4(o[4 * c4], o[4 * c4 + 1], o[4 * c4 + 2], o[4 * c4 + 3]);
-      if (g == 0) {
-        p.part_ml[2 * slot] = M;
-        p.part_ml[2 * slot + 1] = lsum;
-      }
-    } else if (t < p.T) {
-      const float inv = 1.f / fmaxf(lsum, 1e-9f);
-      T* orow = static_cast<T*>(p.out) + (int64_t)b * p.so_b + (int64_t)h * p.so_h + (int64_t)t * p.so_t + c0;
-#pragma unroll
-      for (int c8 = 0; c8 < DC / 8; ++c8) {
-        float f[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = o[c8 * 8 + e] * inv;
-        if constexpr (SPLIT) {
-          float4* o4 = reinterpret_cast<float4*>(orow + c8 * 8);
-          o4[0] = make_float4(f[0], f[1], f[2], f[3]);
-          o4[1] = make_float4(f[4], f[5], f[6], f[7]);
-        } else {
-          Vec<T, 8> w;
-          w.from_float(f);
-          *reinterpret_cast<uint4*>(orow + c8 * 8) = w.w;
-        }
-      }
+    if (t < p.T && partial && g == 0) {
+      p.part_ml[2 * pslot] = M;
+      p.part_ml[2 * pslot + 1] = lsum;
     }
   }
   tc::fence_before_sync();
@@ -904,11 +921,10 @@ __global__ void __launch_bounds__(128) prefill_split_pages_kernel(PfSplitArgs a)
 bool encode_pool_tensor_map(CUtensorMap* map, const void* pool, int64_t rows, int D, int block_size, int dtype);
 
 // epoch: the fp32 variant's number of this call (marks the range flag).
-template <typename T, int D, int BS>
-int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream, uint32_t epoch = 0) {
+template <typename T, int D, int BS, bool PAIR>
+int launch_prefill_tc_impl(const AttnArgs& a, cudaStream_t stream, uint32_t epoch, const PrefillPlan& plan) {
   constexpr bool SPLIT = kPfSplit<T>;
-  using C = PfTcCfg<D, BS, SPLIT>;
-  const PrefillPlan plan = make_prefill_plan(a.B, a.H, a.T, a.D, a.max_pages, BS, a.dtype);
+  using C = PfTcCfg<D, BS, SPLIT, PAIR>;
   if (plan.bytes > 0 && (!a.workspace || a.workspace_bytes < plan.bytes))
     return set_error(B2PA_ERR_WORKSPACE, "paged_prefill: workspace of %zu bytes, %zu needed", a.workspace_bytes,
                      plan.bytes);
@@ -999,7 +1015,7 @@ int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream, uint32_t epoch = 0
   const size_t smem = C::SMEM_FIXED + 4 * (size_t)p.max_cta_pages;
   if (smem > (size_t)device_max_smem_optin())
     return set_error(B2PA_ERR_UNSUPPORTED, "paged_prefill: %d pages per CTA exceed shared memory", p.max_cta_pages);
-  auto kern = paged_prefill_tc_kernel<T, D, BS>;
+  auto kern = paged_prefill_tc_kernel<T, D, BS, PAIR>;
   int rc_attr = set_max_dynamic_smem_cached(reinterpret_cast<const void*>(kern), (int)smem);
   if (rc_attr != B2PA_OK) return rc_attr;
   cudaError_t e;
@@ -1013,6 +1029,17 @@ int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream, uint32_t epoch = 0
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill_tc launch: %s", cudaGetErrorString(e));
   return B2PA_OK;
+}
+
+// The plan decides between the one-CTA-per-SM kernel and, for 16-bit pools
+// with head_dim 64, the two-CTAs-per-SM one (plan.pair).
+template <typename T, int D, int BS>
+int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream, uint32_t epoch = 0) {
+  const PrefillPlan plan = make_prefill_plan(a.B, a.H, a.T, a.D, a.max_pages, BS, a.dtype);
+  if constexpr (!kPfSplit<T> && D == 64) {
+    if (plan.pair) return launch_prefill_tc_impl<T, D, BS, true>(a, stream, epoch, plan);
+  }
+  return launch_prefill_tc_impl<T, D, BS, false>(a, stream, epoch, plan);
 }
 
 }  // namespace b2pa
