@@ -151,9 +151,11 @@ bool prefill_uses_tensor_cores(int D, int block_size, int dtype, int64_t pool_ro
 
 // Split the key range of the tensor-core prefill (query tiles of 128 rows)
 // when the (query tile, head, sequence) CTAs alone would leave SMs idle: the
-// split CTAs fill one wave of `slots` resident CTAs (148 SMs x CTAs per SM),
-// at least 2 key tiles each.  A second wave costs more (combine pass, shared
-// SM) than the shorter key walks save.  Sets kt_per_split / nsplit_max and
+// split CTAs fill one wave of `slots` resident CTAs (148 SMs, one CTA each),
+// at least 2 key tiles each.  Measured on config[2]: a second wave, or a
+// second resident CTA per SM (a 99 KB, one-softmax-group variant sized for
+// two per SM was built and ran 19.4 -> 31.7 us), costs more than the shorter
+// key walks save.  Sets kt_per_split / nsplit_max and
 // the partials' workspace offsets; returns the partials' bytes.
 static size_t tc_key_split(PrefillPlan& pl, int B, int H, int T, int D, int64_t ktmax, int64_t slots,
                            int64_t kt_cap) {
@@ -189,7 +191,6 @@ static PrefillPlan empty_prefill_plan(int64_t ktmax) {
   pl.kt_per_split = (int)(ktmax > 0 ? ktmax : 1);
   pl.nsplit_max = 1;
   pl.split_tc = 0;
-  pl.pair = 0;
   pl.off_part_ml = pl.off_part_o = pl.off_split_k = pl.off_split_v = pl.off_slots = pl.off_flag = 0;
   pl.bytes = 0;
   return pl;
@@ -237,10 +238,7 @@ PrefillPlan make_prefill_plan(int B, int H, int T, int D, int max_pages, int blo
   if (dtype == B2PA_DTYPE_F32 && (D == 64 || D == 128))
     return make_prefill_plan_f32_tiled(B, H, T, D, max_pages, block_size);
   if (!prefill_uses_tensor_cores(D, block_size, dtype, 0)) return pl;
-  // 16-bit head_dim 64: two CTAs per SM (their shared memory allows block
-  // ids of up to 900 key tiles per CTA at that occupancy)
-  pl.pair = D == 64 ? 1 : 0;
-  pl.bytes = pl.pair ? tc_key_split(pl, B, H, T, D, ktmax, 2 * 148, 900) : tc_key_split(pl, B, H, T, D, ktmax, 148, 1024);
+  pl.bytes = tc_key_split(pl, B, H, T, D, ktmax, 148, 1024);
   return pl;
 }
 

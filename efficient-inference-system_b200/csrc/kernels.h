@@ -132,7 +132,6 @@ struct PrefillPlan {
   int kt_per_split;  // 64-key tiles per CTA
   int nsplit_max;
   int split_tc;      // fp32 on the tensor cores: pages split into fp16 hi/lo in the workspace
-  int pair;          // 16-bit head_dim 64 on the tensor cores: two CTAs per SM
   // split_tc: split pages, slot table and the out-of-range flag
   size_t off_part_ml, off_part_o, off_split_k, off_split_v, off_slots, off_flag, bytes;
 };

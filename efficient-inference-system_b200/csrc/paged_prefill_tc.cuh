@@ -112,13 +112,7 @@ __device__ __forceinline__ void prefill_tile_range(const PfTcParams& p, int b, i
 // the general fp32 CUDA-core kernel, launched after this one as a backup that
 // does nothing otherwise.  The K/V pages are split into a workspace copy
 // beforehand (prefill_split_pages_kernel); q and P are split in the kernel.
-// PAIR: the 16-bit head_dim-64 kernel sized to run two CTAs per SM (one
-// softmax warpgroup, 3-stage rings: ~99 KB of shared memory and 256 TMEM
-// columns each), so that a key range split in two keeps every SM busy with
-// two independent tile chains; the per-tile chain (page loads, the Q.K^T /
-// softmax / P.V hand-overs) is latency-bound, so two chains per SM run at
-// nearly twice the rate of one.
-template <int D, int BS, bool SPLIT = false, bool PAIR = false>
+template <int D, int BS, bool SPLIT = false>
 struct PfTcCfg {
   static constexpr int BM = 128;         // query rows per CTA (UMMA M)
   static constexpr int BN = 64;          // keys per tile
@@ -131,13 +125,12 @@ struct PfTcCfg {
   // softmax warps on every SM sub-partition, so one warp's exponentials
   // overlap the other's TMEM loads, barrier waits and P stores.
   // (The fp32 variant, with twice the operand bytes, keeps one group.)
-  static constexpr int NG = !SPLIT && D == 64 && !PAIR ? 2 : 1;
-  static constexpr int CTAS_PER_SM = PAIR ? 2 : 1;
+  static constexpr int NG = !SPLIT && D == 64 ? 2 : 1;
   static constexpr int NSLOT = 2 * NG;  // S/P buffers: two per group
   // Depth of the K ring and of the V ring.  A K stage is refilled once the
   // Q.K^T that read it is done, a V stage once its P.V is done, so each ring
   // loads up to STAGES tiles ahead of its consumer.
-  static constexpr int STAGES = SPLIT ? 3 : (D == 64 ? (PAIR ? 3 : 6) : 4);
+  static constexpr int STAGES = SPLIT ? 3 : (D == 64 ? 6 : 4);
   static constexpr int Q_TILE = BM * D * 2;   // one bf16 / fp16 tile
   static constexpr int KV_TILE = BN * D * 2;
   static constexpr int P_TILE = BM * BN * 2;
@@ -166,8 +159,6 @@ struct PfTcCfg {
   static constexpr int THREADS = SOFTMAX_THREADS + 128;
   static_assert(D == 64 || D == 128, "tcgen05 prefill is built for head_dim 64 and 128");
   static_assert(!SPLIT || D == 64, "the fp32 variant fits shared memory for head_dim 64 only");
-  static_assert(!PAIR || (D == 64 && !SPLIT), "two CTAs per SM: 16-bit head_dim 64 only");
-  static_assert(!PAIR || (SMEM_FIXED <= 100 * 1024 && TMEM_COLS == 256), "two CTAs per SM must fit");
   static_assert(BN % BS == 0 && 32 % PAGES == 0, "block size must divide the key tile");
   static_assert(TMEM_USED <= 512, "TMEM holds 512 columns");
   static_assert(SMEM_FIXED <= 200 * 1024, "shared-memory plan");
@@ -239,13 +230,12 @@ __device__ __forceinline__ void split_f16x8(const float (&f)[8], uint4& hi, uint
   lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
-template <typename T, int D, int BS, bool PAIR = false>
-__global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>, PAIR>::THREADS,
-                                  PfTcCfg<D, BS, kPfSplit<T>, PAIR>::CTAS_PER_SM)
+template <typename T, int D, int BS>
+__global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
                             PfTcParams p) {
   constexpr bool SPLIT = kPfSplit<T>;
-  using C = PfTcCfg<D, BS, SPLIT, PAIR>;
+  using C = PfTcCfg<D, BS, SPLIT>;
   constexpr int NG = C::NG, NSLOT = C::NSLOT;
   extern __shared__ unsigned char smem_raw[];
   unsigned char* smem =
@@ -921,10 +911,11 @@ __global__ void __launch_bounds__(128) prefill_split_pages_kernel(PfSplitArgs a)
 bool encode_pool_tensor_map(CUtensorMap* map, const void* pool, int64_t rows, int D, int block_size, int dtype);
 
 // epoch: the fp32 variant's number of this call (marks the range flag).
-template <typename T, int D, int BS, bool PAIR>
-int launch_prefill_tc_impl(const AttnArgs& a, cudaStream_t stream, uint32_t epoch, const PrefillPlan& plan) {
+template <typename T, int D, int BS>
+int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream, uint32_t epoch = 0) {
   constexpr bool SPLIT = kPfSplit<T>;
-  using C = PfTcCfg<D, BS, SPLIT, PAIR>;
+  using C = PfTcCfg<D, BS, SPLIT>;
+  const PrefillPlan plan = make_prefill_plan(a.B, a.H, a.T, a.D, a.max_pages, BS, a.dtype);
   if (plan.bytes > 0 && (!a.workspace || a.workspace_bytes < plan.bytes))
     return set_error(B2PA_ERR_WORKSPACE, "paged_prefill: workspace of %zu bytes, %zu needed", a.workspace_bytes,
                      plan.bytes);
@@ -1015,7 +1006,7 @@ int launch_prefill_tc_impl(const AttnArgs& a, cudaStream_t stream, uint32_t epoc
   const size_t smem = C::SMEM_FIXED + 4 * (size_t)p.max_cta_pages;
   if (smem > (size_t)device_max_smem_optin())
     return set_error(B2PA_ERR_UNSUPPORTED, "paged_prefill: %d pages per CTA exceed shared memory", p.max_cta_pages);
-  auto kern = paged_prefill_tc_kernel<T, D, BS, PAIR>;
+  auto kern = paged_prefill_tc_kernel<T, D, BS>;
   int rc_attr = set_max_dynamic_smem_cached(reinterpret_cast<const void*>(kern), (int)smem);
   if (rc_attr != B2PA_OK) return rc_attr;
   cudaError_t e;
@@ -1029,17 +1020,6 @@ int launch_prefill_tc_impl(const AttnArgs& a, cudaStream_t stream, uint32_t epoc
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill_tc launch: %s", cudaGetErrorString(e));
   return B2PA_OK;
-}
-
-// The plan decides between the one-CTA-per-SM kernel and, for 16-bit pools
-// with head_dim 64, the two-CTAs-per-SM one (plan.pair).
-template <typename T, int D, int BS>
-int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream, uint32_t epoch = 0) {
-  const PrefillPlan plan = make_prefill_plan(a.B, a.H, a.T, a.D, a.max_pages, BS, a.dtype);
-  if constexpr (!kPfSplit<T> && D == 64) {
-    if (plan.pair) return launch_prefill_tc_impl<T, D, BS, true>(a, stream, epoch, plan);
-  }
-  return launch_prefill_tc_impl<T, D, BS, false>(a, stream, epoch, plan);
 }
 
 }  // namespace b2pa
