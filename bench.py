@@ -925,14 +925,50 @@ def measure_secondary(torch, lib, _lib, dev, workload: str, dtype, steps: int, w
     torch.cuda.synchronize()
     attn_ms = float(np.mean([a.elapsed_time(b) for a, b in gev]))
     del g
+    # Per-call device time without the graph launch and event overhead of a
+    # single replay (~6 us on this part even for a trivial kernel): a graph of
+    # 10 x (L2 flush, attention call) minus a graph of the 10 flushes alone.
+    def graph_of(n, with_attention):
+        gg = torch.cuda.CUDAGraph()
+        s2 = torch.cuda.Stream()
+        s2.wait_stream(torch.cuda.current_stream())
+        nonlocal sh
+        with torch.cuda.stream(s2):
+            sh = s2.cuda_stream
+            with torch.cuda.graph(gg, stream=s2):
+                for _ in range(n):
+                    flush.zero_()
+                    if with_attention:
+                        attend()
+        torch.cuda.current_stream().wait_stream(s2)
+        sh = torch.cuda.current_stream(dev).cuda_stream
+        return gg
+
+    def replay_ms(gg, reps=5):
+        ts = []
+        for _ in range(reps):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            gg.replay()
+            b.record()
+            torch.cuda.synchronize()
+            ts.append(a.elapsed_time(b))
+        return float(np.median(ts))
+
+    g_both, g_flush = graph_of(10, True), graph_of(10, False)
+    attn_in_graph_ms = (replay_ms(g_both) - replay_ms(g_flush)) / 10
+    del g_both, g_flush
     es = 2 if dtype == torch.bfloat16 else 4
     kv_bytes = 2 * Hs * Ds * es * int(lens.sum())
     line = {"workload": workload, "dtype": str(dtype).replace("torch.", ""), "steps": steps,
             "config": {"B": B, "H": Hs, "D": Ds, "T": T, "block_size": bs, "pool_blocks": NB,
                        "l2": "flushed before every step (256 MB written, then 256 MB read)"},
             "ms_per_step_append_plus_attention": step_ms, "attention_ms": attn_ms,
+            "attention_ms_in_graph": attn_in_graph_ms,
             "attention_ms_eager_call": attn_eager_ms, "append_ms": step_ms - attn_eager_ms,
-            "timing": "attention_ms: CUDA-graph replay (device time); eager: per-call incl. host launch"}
+            "timing": "attention_ms: one CUDA-graph replay of the call between two events (device time, incl. the "
+                      "replay's launch overhead); attention_ms_in_graph: per call inside a graph of 10 flushed "
+                      "calls, minus the flushes; eager: per-call incl. host launch"}
     if T > 1:
         flops = _prefill_flops(prefix, T, Hs, Ds)
         bytes_ = kv_bytes + 2 * B * Hs * T * Ds * es
@@ -940,6 +976,9 @@ def measure_secondary(torch, lib, _lib, dev, workload: str, dtype, steps: int, w
                      "ms_per_step_fused_append_prefill": fused_ms,
                      "tokens_per_s_fused": B * T / (fused_ms / 1e3),
                      "attention_tflops": flops / (attn_ms / 1e3) / 1e12,
+                     "attention_tflops_in_graph": flops / (attn_in_graph_ms / 1e3) / 1e12,
+                     "frac_of_bf16_tensor_peak_in_graph": flops / (attn_in_graph_ms / 1e3) / 1e12
+                     / peaks["bf16_tflops"],
                      "flops_per_launch": flops, "bytes_per_launch": bytes_,
                      "attention_hbm_gbs": bytes_ / (attn_ms / 1e3) / 1e9,
                      "frac_of_bf16_tensor_peak": flops / (attn_ms / 1e3) / 1e12 / peaks["bf16_tflops"],
@@ -950,6 +989,7 @@ def measure_secondary(torch, lib, _lib, dev, workload: str, dtype, steps: int, w
                      "ms_per_step_fused_append_decode": fused_ms,
                      "tokens_per_s_fused": B / (fused_ms / 1e3),
                      "attention_hbm_gbs": bytes_ / (attn_ms / 1e3) / 1e9,
+                     "attention_hbm_gbs_in_graph": bytes_ / (attn_in_graph_ms / 1e3) / 1e9,
                      "bytes_per_launch": bytes_,
                      "frac_of_hbm_peak": bytes_ / (attn_ms / 1e3) / 1e9 / peaks["hbm_gbs"]})
     if cpu_seconds is not None:
@@ -989,7 +1029,9 @@ def secondary_summary(args) -> dict:
 
     dev = torch.device("cuda", 0)
     lib = _lib.load()
-    keep = ("attention_ms", "attention_tflops", "frac_of_bf16_tensor_peak", "frac_of_hbm_peak",
+    keep = ("attention_ms", "attention_ms_in_graph", "attention_tflops", "attention_tflops_in_graph",
+            "frac_of_bf16_tensor_peak", "frac_of_bf16_tensor_peak_in_graph", "attention_hbm_gbs_in_graph",
+            "frac_of_hbm_peak",
             "attention_hbm_gbs", "ms_per_step_append_plus_attention", "ms_per_step_fused_append_prefill",
             "ms_per_step_fused_append_decode", "tokens_per_s_fused")
     out = {}
@@ -1002,8 +1044,9 @@ def secondary_summary(args) -> dict:
         line = measure_secondary(torch, lib, _lib, dev, workload, dtype, max(args.steps, 10), args.warmup,
                                  None, plen)
         out[name] = {k: line[k] for k in keep if k in line}
-    out["timing"] = ("CUDA events; L2 flushed before every step; attention_ms is a CUDA-graph replay of the "
-                     "attention call (device time), the step times are eager calls")
+    out["timing"] = ("CUDA events; L2 flushed before every call; attention_ms: one CUDA-graph replay of the call "
+                     "(includes ~6 us of replay launch overhead); attention_ms_in_graph: per call inside a graph of "
+                     "10 flushed calls minus the flushes; step times: eager calls")
     return out
 
 

@@ -767,6 +767,8 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
 // Serves both prefill kernels (p.bm gives their query-tile height).
 template <typename T, int D, int BS>
 __global__ void __launch_bounds__(256) prefill_combine_kernel(PfTcParams p) {
+  // launched as a programmatic dependent of the kernel that wrote the partials
+  pdl_wait();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * 8 + warp;
   if (row >= (int64_t)p.B * p.H * p.T) return;
@@ -1015,7 +1017,8 @@ int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream, uint32_t epoch = 0
   if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill_tc launch: %s", cudaGetErrorString(e));
   if (plan.nsplit_max > 1) {
     const int64_t rows = (int64_t)a.B * a.H * a.T;
-    prefill_combine_kernel<T, D, BS><<<(unsigned)((rows + 7) / 8), 256, 0, stream>>>(p);
+    e = launch_pdl(prefill_combine_kernel<T, D, BS>, dim3((unsigned)((rows + 7) / 8)), dim3(256), 0, stream, p);
+    if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "prefill_combine launch: %s", cudaGetErrorString(e));
   }
   e = cudaGetLastError();
   if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill_tc launch: %s", cudaGetErrorString(e));
