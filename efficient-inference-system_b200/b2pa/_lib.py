@@ -59,6 +59,10 @@ SIGNATURES: dict[str, tuple] = {
     "b2pa_zero_blocks": (_I, [_VP, _VP, _I64P, _I64, _VP, _I, _I, _I, _I, _I, _VP, _VP]),
     "b2pa_patch_table": (_I, [_VP, _I64, _VP, _I, _VP, _VP]),
     "b2pa_selftest_wait_timeout": (_I, [_VP, _VP, _VP]),
+    "b2pa_rows_linear": (_I, [_VP, _I64, _I, _I, _VP, _VP, ctypes.c_float, _VP, _VP, _I, _I, _VP, _I64, _I,
+                              _VP, _VP]),
+    "b2pa_rows_embed": (_I, [_VP, _VP, _I, _VP, _I64, _VP, _I64, _I, _VP, _I64, _VP, _VP]),
+    "b2pa_rows_argmax": (_I, [_VP, _I64, _I, _I, _VP, _VP, _VP]),
 }
 
 _lock = threading.Lock()

@@ -295,6 +295,48 @@ B2PA_API int b2pa_patch_table(int32_t* table, int64_t n_cells, const int32_t* pa
  */
 B2PA_API int b2pa_selftest_wait_timeout(int32_t* status, int32_t* done, void* stream);
 
+/*
+ * The non-attention operations of a decode step, fp32, for M <= 16 rows (the
+ * batch's new tokens).  In the reference they are torch modules of the
+ * model: nn.LayerNorm, nn.Linear and nn.GELU of TransformerBlock
+ * (src/model/transformer.py:10-18,27-34), the q/k/v and output projections of
+ * CausalSelfAttention (src/model/attention.py:46-48,64), the embeddings, final
+ * LayerNorm and lm_head of TinyTransformerLM (src/model/transformer.py:
+ * 150,179-180) and the greedy torch.argmax of generation
+ * (src/inference/generate_with_cache.py:204).  With M rows every product is
+ * a matrix-vector product bound by reading the weights, so each call reads
+ * its weight matrix once, with the row-wise work fused around it.
+ *
+ * b2pa_rows_linear: for each row m < M of x ([M, K], row stride
+ * x_row_stride), xn = LayerNorm(x[m]) with ln_weight / ln_bias / ln_eps when
+ * ln_weight is not NULL (ln_bias may be NULL), else x[m]; then
+ * r[n] = xn . weight[n, :] + bias[n] (weight [N, K] row-major; bias may be
+ * NULL), GELU (erf form) when activation == 1; y[m, n] = r[n], or
+ * y[m, n] += r[n] when accumulate (a residual add).  y must not overlap x.
+ * K a multiple of 4, M * K <= 32768, x / weight / LayerNorm vectors 16-byte
+ * aligned with 16-byte row strides.
+ */
+B2PA_API int b2pa_rows_linear(const float* x, int64_t x_row_stride, int M, int K,
+                              const float* ln_weight, const float* ln_bias, float ln_eps,
+                              const float* weight, const float* bias, int N, int activation,
+                              float* y, int64_t y_row_stride, int accumulate,
+                              int32_t* status, void* stream);
+
+/*
+ * x[m, :] = token_table[token_ids[m], :] + position_table[positions[m], :]
+ * for m < M (int64 ids on the device; tables [vocab, K] and
+ * [max_positions, K], K a multiple of 4).  An id outside its table writes a
+ * zero row and sets B2PA_ERR_INVALID_ARGUMENT in *status.
+ */
+B2PA_API int b2pa_rows_embed(const int64_t* token_ids, const int64_t* positions, int M,
+                             const float* token_table, int64_t vocab,
+                             const float* position_table, int64_t max_positions, int K,
+                             float* x, int64_t x_row_stride, int32_t* status, void* stream);
+
+/* out[m] = the first index of the largest of x[m, 0:N] (int64), m < M. */
+B2PA_API int b2pa_rows_argmax(const float* x, int64_t x_row_stride, int M, int N, int64_t* out,
+                              int32_t* status, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif
