@@ -41,16 +41,19 @@ class SharedStepMetadata:
     int32 ``[table (B x width) | seq_lens | start_pos | ones]`` and the int64
     lengths ``append_batch`` returns."""
 
+    RING = 4  # pinned host copies: the host may plan this many steps ahead of the GPU
+
     def __init__(self, device: torch.device, B: int, width: int):
         self.device, self.B, self.width = device, B, width
         n = B * width + 3 * B
         self.dev = torch.empty(n, dtype=torch.int32, device=device)
-        self.host = torch.empty(n, dtype=torch.int32, pin_memory=True)
-        self.host_np = self.host.numpy()
-        self.host_np[B * width + 2 * B:] = 1
+        self.hosts = [torch.empty(n, dtype=torch.int32, pin_memory=True) for _ in range(self.RING)]
+        for h in self.hosts:
+            h.numpy()[B * width + 2 * B:] = 1
+        self.events = [torch.cuda.Event() for _ in range(self.RING)]
+        self.recorded = [False] * self.RING
+        self.slot = 0
         self.seq_out = torch.empty(B, dtype=torch.int64, device=device)
-        self.copied = torch.cuda.Event()
-        self.pending_copy = False
         self.workspace: torch.Tensor | None = None
 
     @property
@@ -74,21 +77,27 @@ class SharedStepMetadata:
         return self._row(2)
 
     def upload(self, tables: list, seq_lens: list[int], starts: list[int]) -> None:
-        """Writes the step's table and rows; one copy on the current stream.
-        The pinned buffer is rewritten only once the previous copy is done."""
-        if self.pending_copy:
-            self.copied.synchronize()
+        """Writes the step's table and rows; one copy on the current stream,
+        from the next pinned buffer of a small ring (rewritten only once the
+        copy that last read it is done, so the host can plan a few steps ahead
+        of the GPU without waiting)."""
+        i = self.slot
+        self.slot = (i + 1) % self.RING
+        if self.recorded[i]:
+            self.events[i].synchronize()
+        host = self.hosts[i]
+        h = host.numpy()
         B, W = self.B, self.width
-        t = self.host_np[: B * W].reshape(B, W)
+        t = h[: B * W].reshape(B, W)
         t.fill(-1)
         for r, ids in enumerate(tables):
             if ids:
                 t[r, : len(ids)] = ids
-        self.host_np[B * W: B * W + B] = seq_lens
-        self.host_np[B * W + B: B * W + 2 * B] = starts
-        self.dev.copy_(self.host, non_blocking=True)
-        self.copied.record()
-        self.pending_copy = True
+        h[B * W: B * W + B] = seq_lens
+        h[B * W + B: B * W + 2 * B] = starts
+        self.dev.copy_(host, non_blocking=True)
+        self.events[i].record()
+        self.recorded[i] = True
 
     def ensure_workspace(self, H: int, D: int, block_size: int, dtype: torch.dtype) -> torch.Tensor:
         lib = _lib.load()

@@ -149,9 +149,6 @@ def test_fused_decoder_config0(cuda_device):
             np.testing.assert_allclose(logits[s].numpy(), logits_m[s].numpy(), rtol=1e-4, atol=1e-5)
     assert results["graph"][3].captures == 1
     assert b2pa.read_status(cuda_device) == 0
-    print(json.dumps({"config": "BASELINE config[0] decode on b2pa kernels only (FusedDecoder), 127 steps, batch 1",
-                      "eager_tokens_per_s": 127 / results["eager"][2], "graph_tokens_per_s": 127 / results["graph"][2],
-                      "graph_ms_per_token": results["graph"][2] / 127 * 1e3}))
 
 
 @torch.no_grad()
@@ -200,3 +197,58 @@ def test_fused_decoder_batched_ragged(cuda_device):
     for a, b in zip(outs[0][1], outs[1][1]):
         np.testing.assert_allclose(b.numpy(), a.numpy(), rtol=1e-4, atol=1e-5)
     assert b2pa.read_status(cuda_device) == 0
+
+
+@torch.no_grad()
+def test_decode_step_throughput_config0(cuda_device):
+    """config[0] decode (127 greedy steps after the prompt, batch 1) four
+    ways, with the tokens kept on the device and one synchronisation at the
+    end: the model's own step (torch modules + b2pa attention), the same as a
+    CUDA graph, FusedDecoder, and FusedDecoder as a CUDA graph.  Tokens must
+    equal the reference's (golden) every way; prints tokens/s."""
+    import b2pa
+
+    gold = load_golden("model_config0")["tokens"]
+    prev = b2pa.set_fused_append(True)
+    report = {"config": "BASELINE config[0] decode: 127 greedy steps after the 128-token prompt, batch 1, FP32; "
+                        "tokens kept on the device, one host synchronisation at the end"}
+    try:
+        for name in ("model_eager", "model_graph", "fused_eager", "fused_graph", "model_eager", "model_graph",
+                     "fused_eager", "fused_graph"):
+            model, prompt = om.config0_model(om.b2pa_backend(), cuda_device)
+            nxt, caches = _prefill(model, prompt)
+            layer_states = [[c] for c in caches]
+            batches = [model.backend.batch_cls(states=[c], pool=c.pool) for c in caches]
+            ids = nxt.clone()
+            pos = torch.zeros(1, dtype=torch.int64, device=cuda_device)
+            toks = torch.empty(1, 128, dtype=torch.int64, device=cuda_device)
+            toks[:, 0] = nxt
+            if name.startswith("fused"):
+                dec = b2pa.FusedDecoder(model, max_batch=1)
+                step_fn = lambda: dec.step(ids, pos, batches)[1]
+            else:
+                def step_fn():
+                    logits, _ = model(ids.view(1, 1), kv_caches=batches, position_offset=pos, current_lengths=1)
+                    return torch.argmax(logits[:, -1, :], dim=-1)
+            graph = b2pa.DecodeGraph(step_fn) if name.endswith("graph") else None
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            for s in range(1, 128):
+                pos.fill_(128 + s - 1)
+                if graph is not None:
+                    nx = graph(layer_states)
+                elif name.startswith("fused"):
+                    with b2pa.DecodeStep(layer_states):
+                        nx = step_fn()
+                else:
+                    nx = step_fn()
+                toks[:, s] = nx
+                ids.copy_(nx)
+            torch.cuda.synchronize()
+            secs = time.perf_counter() - t0
+            assert np.array_equal(toks.cpu().numpy(), gold), name
+            report[name + "_tokens_per_s"] = 127 / secs  # the second (warm) run of each way is kept
+    finally:
+        b2pa.set_fused_append(prev)
+    assert b2pa.read_status(cuda_device) == 0
+    print(json.dumps(report))
