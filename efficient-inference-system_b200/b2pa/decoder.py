@@ -32,6 +32,32 @@ import torch
 from . import _lib
 
 
+def collect_parameters(model) -> dict:
+    """The decode step's parameters of a TinyTransformerLM-shaped model, read
+    through the reference's module names (src/model/transformer.py:7-18,
+    38-181; src/model/attention.py:9-30): embeddings, per block the two
+    LayerNorms, the q/k/v weights concatenated into one [3d, d] matrix, the
+    output projection and the two MLP layers, then the final LayerNorm and
+    lm_head."""
+    layers = []
+    for blk in model.blocks:
+        att = blk.attn
+        layers.append({
+            "ln1": (blk.ln1.weight.detach(), blk.ln1.bias.detach(), float(blk.ln1.eps)),
+            "w_qkv": torch.cat([att.q_proj.weight, att.k_proj.weight, att.v_proj.weight]).detach().contiguous(),
+            "b_qkv": torch.cat([att.q_proj.bias, att.k_proj.bias, att.v_proj.bias]).detach().contiguous(),
+            "w_o": att.out_proj.weight.detach(), "b_o": att.out_proj.bias.detach(),
+            "ln2": (blk.ln2.weight.detach(), blk.ln2.bias.detach(), float(blk.ln2.eps)),
+            "w1": blk.mlp[0].weight.detach(), "b1": blk.mlp[0].bias.detach(),
+            "w2": blk.mlp[2].weight.detach(), "b2": blk.mlp[2].bias.detach(),
+            "H": att.num_heads,
+        })
+    return {"tok": model.token_emb.weight.detach(), "pos": model.pos_emb.weight.detach(), "layers": layers,
+            "ln_f": (model.ln_f.weight.detach(), model.ln_f.bias.detach(), float(model.ln_f.eps)),
+            "w_head": model.lm_head.weight.detach(),
+            "b_head": model.lm_head.bias.detach() if model.lm_head.bias is not None else None}
+
+
 class FusedDecoder:
     """Decode steps of a TinyTransformerLM-shaped fp32 model, up to
     ``max_batch`` (<= 16) requests per step."""
@@ -43,28 +69,12 @@ class FusedDecoder:
         if w.dtype != torch.float32 or not w.is_cuda:
             raise TypeError("b2pa.FusedDecoder: the model must be fp32 on a CUDA device")
         self.device = w.device
-        self.d = model.token_emb.weight.shape[1]
-        self.vocab = model.lm_head.weight.shape[0]
-        self.tok = model.token_emb.weight.detach()
-        self.pos = model.pos_emb.weight.detach()
-        self.layers = []
-        for blk in model.blocks:
-            att = blk.attn
-            H = att.num_heads
-            self.layers.append({
-                "ln1": (blk.ln1.weight.detach(), blk.ln1.bias.detach(), float(blk.ln1.eps)),
-                "w_qkv": torch.cat([att.q_proj.weight, att.k_proj.weight, att.v_proj.weight]).detach().contiguous(),
-                "b_qkv": torch.cat([att.q_proj.bias, att.k_proj.bias, att.v_proj.bias]).detach().contiguous(),
-                "w_o": att.out_proj.weight.detach(), "b_o": att.out_proj.bias.detach(),
-                "ln2": (blk.ln2.weight.detach(), blk.ln2.bias.detach(), float(blk.ln2.eps)),
-                "w1": blk.mlp[0].weight.detach(), "b1": blk.mlp[0].bias.detach(),
-                "w2": blk.mlp[2].weight.detach(), "b2": blk.mlp[2].bias.detach(),
-                "H": H,
-            })
+        P = collect_parameters(model)
+        self.tok, self.pos, self.layers = P["tok"], P["pos"], P["layers"]
+        self.ln_f, self.w_head, self.b_head = P["ln_f"], P["w_head"], P["b_head"]
+        self.d = self.tok.shape[1]
+        self.vocab = self.w_head.shape[0]
         self.d_ff = self.layers[0]["w1"].shape[0] if self.layers else 0
-        self.ln_f = (model.ln_f.weight.detach(), model.ln_f.bias.detach(), float(model.ln_f.eps))
-        self.w_head = model.lm_head.weight.detach()
-        self.b_head = model.lm_head.bias.detach() if model.lm_head.bias is not None else None
         for t in [self.tok, self.pos, self.w_head] + [v for L in self.layers for v in L.values()
                                                        if isinstance(v, torch.Tensor)]:
             if not t.is_contiguous():
