@@ -248,6 +248,16 @@ def test_decode_step_throughput_config0(cuda_device):
             secs = time.perf_counter() - t0
             assert np.array_equal(toks.cpu().numpy(), gold), name
             report[name + "_tokens_per_s"] = 127 / secs  # the second (warm) run of each way is kept
+            if graph is not None:
+                # device time of one step: the captured step replayed back to back (it rewrites the
+                # last step's rows with the same values and recomputes the same outputs)
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                a.record()
+                for _ in range(50):
+                    graph.graph.replay()
+                b.record()
+                torch.cuda.synchronize()
+                report[name + "_device_us_per_step"] = a.elapsed_time(b) / 50 * 1e3
     finally:
         b2pa.set_fused_append(prev)
     assert b2pa.read_status(cuda_device) == 0
