@@ -29,11 +29,13 @@ out the same block ids.  Here that is checked, not assumed, and used:
 """
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
 
 from . import _lib
+from ._staging import _cudart, _rt_check
 
 
 class SharedStepMetadata:
@@ -50,11 +52,19 @@ class SharedStepMetadata:
         self.hosts = [torch.empty(n, dtype=torch.int32, pin_memory=True) for _ in range(self.RING)]
         for h in self.hosts:
             h.numpy()[B * width + 2 * B:] = 1
-        self.events = [torch.cuda.Event() for _ in range(self.RING)]
+        rt = _cudart()
+        self.events = []
+        with torch.cuda.device(device):
+            for _ in range(self.RING):
+                ev = ctypes.c_void_p()
+                _rt_check(rt.cudaEventCreateWithFlags(ctypes.byref(ev), 2), "cudaEventCreateWithFlags")
+                self.events.append(ev)
         self.recorded = [False] * self.RING
         self.slot = 0
+        self.nbytes = 4 * n
         self.seq_out = torch.empty(B, dtype=torch.int64, device=device)
         self.workspace: torch.Tensor | None = None
+        self._ws_key = None
 
     @property
     def table(self) -> torch.Tensor:
@@ -83,8 +93,9 @@ class SharedStepMetadata:
         of the GPU without waiting)."""
         i = self.slot
         self.slot = (i + 1) % self.RING
+        rt = _cudart()
         if self.recorded[i]:
-            self.events[i].synchronize()
+            _rt_check(rt.cudaEventSynchronize(self.events[i]), "cudaEventSynchronize")
         host = self.hosts[i]
         h = host.numpy()
         B, W = self.B, self.width
@@ -95,11 +106,16 @@ class SharedStepMetadata:
                 t[r, : len(ids)] = ids
         h[B * W: B * W + B] = seq_lens
         h[B * W + B: B * W + 2 * B] = starts
-        self.dev.copy_(host, non_blocking=True)
-        self.events[i].record()
+        stream = _lib.stream_handle(self.device)
+        _rt_check(rt.cudaMemcpyAsync(self.dev.data_ptr(), host.data_ptr(), self.nbytes, 1, stream), "cudaMemcpyAsync")
+        _rt_check(rt.cudaEventRecord(self.events[i], stream), "cudaEventRecord")
         self.recorded[i] = True
 
     def ensure_workspace(self, H: int, D: int, block_size: int, dtype: torch.dtype) -> torch.Tensor:
+        key = (H, D, block_size, dtype)
+        if key == self._ws_key:
+            return self.workspace
+        self._ws_key = key
         lib = _lib.load()
         need = lib.b2pa_paged_decode_workspace_size(self.B, H, D, self.width, block_size, _lib.dtype_code(dtype))
         if self.workspace is None or self.workspace.numel() < need:

@@ -11,8 +11,10 @@
 // streams whole weight rows (coalesced 16-byte loads, no L1 allocation) and
 // dots them against every staged row, so the weights are read exactly once.
 // Two more kernels gather the token + position embeddings and take the
-// argmax over the vocabulary.  All are launched as programmatic dependents
-// (they wait for the kernel before them before reading anything).
+// argmax over the vocabulary.  All are launched as programmatic dependents:
+// they wait for the kernel before them before reading its results (the
+// linear kernel requests the first pieces of its weight rows before waiting,
+// since the weights never depend on that kernel).
 //
 // Numerics: fp32 throughout, FMA accumulation; LayerNorm as torch computes it
 // (biased variance, rsqrt(var + eps)); GELU exact, 0.5 x (1 + erf(x / sqrt 2)),
@@ -62,11 +64,23 @@ __device__ __forceinline__ float warp_sum(float v) {
 template <int MAXM>
 __global__ void __launch_bounds__(kRowsWarps * 32) rows_linear_kernel(RowsLinearArgs a) {
   extern __shared__ float4 xs4[];  // [M][K/4]
-  pdl_wait();
-  pdl_launch_dependents();
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int K4 = a.K >> 2;
   const int M = a.M;
+  const int n = blockIdx.x * kRowsWarps + warp;
+  const bool active = n < a.N;
+  const float4* wrow = reinterpret_cast<const float4*>(a.w + (int64_t)(active ? n : 0) * a.K);
+  // The weights do not depend on the kernel before this one: the first 128
+  // 16-byte pieces of this warp's weight row are requested before waiting
+  // for it, so their latency overlaps its tail.
+  float4 w0[4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int k = lane + 32 * u;
+    w0[u] = (active && k < K4) ? ld_stream(wrow + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  pdl_wait();
+  pdl_launch_dependents();
   for (int i = tid; i < M * K4; i += blockDim.x) {
     const int m = i / K4, k4 = i - m * K4;
     xs4[i] = *reinterpret_cast<const float4*>(a.x + (int64_t)m * a.xs + 4 * k4);
@@ -100,14 +114,25 @@ __global__ void __launch_bounds__(kRowsWarps * 32) rows_linear_kernel(RowsLinear
     }
     __syncthreads();
   }
-  const int n = blockIdx.x * kRowsWarps + warp;
-  if (n >= a.N) return;
-  const float4* wrow = reinterpret_cast<const float4*>(a.w + (int64_t)n * a.K);
+  if (!active) return;
   float acc[MAXM];
 #pragma unroll
   for (int m = 0; m < MAXM; ++m) acc[m] = 0.f;
-  // four weight loads in flight per lane before the dot products
-  int k4 = lane;
+  // the prefetched pieces, then four loads in flight per lane at a time
+#pragma unroll
+  for (int u = 0; u < 4; ++u) {
+    const int k = lane + 32 * u;
+    if (k < K4) {
+#pragma unroll
+      for (int m = 0; m < MAXM; ++m) {
+        if (m < M) {
+          const float4 xv = xs4[(int64_t)m * K4 + k];
+          acc[m] = fmaf(w0[u].x, xv.x, fmaf(w0[u].y, xv.y, fmaf(w0[u].z, xv.z, fmaf(w0[u].w, xv.w, acc[m]))));
+        }
+      }
+    }
+  }
+  int k4 = lane + 128;
   for (; k4 + 96 < K4; k4 += 128) {
     float4 w[4];
 #pragma unroll
