@@ -19,7 +19,7 @@
 //           from the table, so the first loads leave before the rest of the
 //           CTA has finished setting up;
 //   two MMA issuer warps (one elected lane each): the QK warp issues
-//           S = Q.K^T (M=128, N=64, K=D) into TMEM up to 2*NG tiles ahead of
+//           S = Q.K^T (M=128, N=64, K=D) into TMEM up to NSLOT tiles ahead of
 //           the softmax; the PV warp issues O_g += P.V (M=128, N=D, K=64)
 //           into the TMEM accumulator of the tile's group.  Splitting the
 //           issue halves the serial chain of waits, MMAs and commits per tile
@@ -124,9 +124,11 @@ struct PfTcCfg {
   // accumulator; the groups are merged in the epilogue.  Two groups put two
   // softmax warps on every SM sub-partition, so one warp's exponentials
   // overlap the other's TMEM loads, barrier waits and P stores.
-  // (The fp32 variant, with twice the operand bytes, keeps one group.)
-  static constexpr int NG = !SPLIT && D == 64 ? 2 : 1;
-  static constexpr int NSLOT = 2 * NG;  // S/P buffers: two per group
+  static constexpr int NG = D == 64 ? 2 : 1;
+  // S/P buffers: two per group; one per group for the fp32 variant, whose
+  // hi/lo operand tiles take twice the shared memory (its two groups still
+  // alternate, so one group's softmax overlaps the other's Q.K^T).
+  static constexpr int NSLOT = SPLIT ? NG : 2 * NG;
   // Depth of the K ring and of the V ring.  A K stage is refilled once the
   // Q.K^T that read it is done, a V stage once its P.V is done, so each ring
   // loads up to STAGES tiles ahead of its consumer.
@@ -534,9 +536,11 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
     // P values stay below 2^kRescale and the rescale of O (TMEM load, scale,
     // store) is rare.  Rescaling at the group's i-th tile j waits for the
     // group's previous P.V (tile j - NG): o_full[g] completes one phase per
-    // P.V of the group; the p_free wait before it makes P.V(j - 2*NG) done,
-    // and P.V(j) cannot start before this warp releases P(j), so o_full[g]
-    // is in phase i-1 or i and the parity wait is exact.
+    // P.V of the group; the p_free wait before it makes P.V(j - NSLOT) done
+    // (NSLOT is 2*NG, or NG for the fp32 variant: then that is the group's
+    // previous P.V itself), and P.V(j) cannot start before this warp releases
+    // P(j), so o_full[g] has completed i-1 or i phases and the parity wait
+    // is exact.
     constexpr float kRescale = 8.f;
     // Row maxima are taken on unscaled scores and scaled once (sc > 0); a
     // scale that is not positive is applied to the scores first instead.
