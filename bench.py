@@ -530,10 +530,12 @@ def e2e_leg(torch, b2pa, wl: Workload, dev, lens_now: np.ndarray, warmup: int, s
     + paged_attention) with host buffers: every step uploads its new K, V and
     q (one fused-QKV pinned buffer) and copies its output back to pinned host
     memory, whose arrival the host waits for.  The copies are pipelined as a
-    serving loop would: step i+1's upload runs on a copy stream into a second
+    serving loop would: step i+1's upload runs on a copy stream into another
     device buffer while step i decodes, step i's output goes down on another
     copy stream while step i+1 decodes, and the host waits for step i's
-    output after it has launched step i+1.  Returns device ms for ``steps``."""
+    output after it has launched step i+1 (three input buffers, so that a
+    step's bulk upload never queues ahead of a step's metadata copy).
+    Returns device ms for ``steps``."""
     import torch.distributed as dist
 
     cache = build_public_cache(b2pa, wl, lens_now)
@@ -543,22 +545,27 @@ def e2e_leg(torch, b2pa, wl: Workload, dev, lens_now: np.ndarray, warmup: int, s
     d2h_stream = torch.cuda.Stream(dev)
     host_kvq = torch.randn(B, 1, 3, H, D, dtype=torch.bfloat16).pin_memory()
     host_out = [torch.empty(B, H, 1, D, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
-    dev_kvq = [torch.empty(B, 1, 3, H, D, dtype=torch.bfloat16, device=dev) for _ in range(2)]
-    up_ev = [torch.cuda.Event() for _ in range(2)]
-    free_ev = [torch.cuda.Event() for _ in range(2)]
+    # three input buffers: step i+2's upload goes into step i-1's buffer and
+    # is enqueued once step i-1's output has arrived -- after step i's small
+    # metadata copy on the compute stream, which would otherwise wait behind
+    # the bulk copy in the host-to-device copy engine
+    NBUF = 3
+    dev_kvq = [torch.empty(B, 1, 3, H, D, dtype=torch.bfloat16, device=dev) for _ in range(NBUF)]
+    up_ev = [torch.cuda.Event() for _ in range(NBUF)]
+    free_ev = [torch.cuda.Event() for _ in range(NBUF)]
     out_ev = [torch.cuda.Event() for _ in range(2)]
     for e in free_ev:
         e.record(comp)
 
     def upload(i):
-        j = i % 2
-        copy_stream.wait_event(free_ev[j])          # step i-2 is done reading this buffer
+        j = i % NBUF
+        copy_stream.wait_event(free_ev[j])          # step i-3 is done reading this buffer
         with torch.cuda.stream(copy_stream):
             dev_kvq[j].copy_(host_kvq, non_blocking=True)
         up_ev[j].record(copy_stream)
 
     def compute(i):
-        j = i % 2
+        j, o = i % NBUF, i % 2
         comp.wait_event(up_ev[j])
         k, v, q = (dev_kvq[j][:, :, c].transpose(1, 2) for c in range(3))
         cache.append_batch(k, v, 1)
@@ -567,18 +574,21 @@ def e2e_leg(torch, b2pa, wl: Workload, dev, lens_now: np.ndarray, warmup: int, s
         d2h_stream.wait_event(free_ev[j])
         out.record_stream(d2h_stream)
         with torch.cuda.stream(d2h_stream):
-            host_out[j].copy_(out, non_blocking=True)
-        out_ev[j].record(d2h_stream)
+            host_out[o].copy_(out, non_blocking=True)
+        out_ev[o].record(d2h_stream)
 
     def run(n):
         copy_stream.wait_stream(comp)
-        upload(0)
+        for i in range(min(2, n)):
+            upload(i)
         for i in range(n):
             compute(i)
-            if i + 1 < n:
-                upload(i + 1)
             if i >= 1:
                 out_ev[(i - 1) % 2].synchronize()      # step i-1's output is on the host
+            # enqueued only now, behind step i's metadata copy in the copy
+            # engine; it runs while step i decodes
+            if i + 2 < n:
+                upload(i + 2)
         out_ev[(n - 1) % 2].synchronize()
 
     fused_before = b2pa.set_fused_append(fused)
