@@ -15,7 +15,7 @@ from .attention import (
     paged_attention_prefill_b200,
 )
 from .integration import install_into_reference
-from .decoder import FusedDecoder
+from .decoder import FusedDecodeExecutor, FusedDecoder
 from .step import DecodeGraph, DecodeStep, SharedStepMetadata
 from .serving import ContinuousBatchingRank, LeastOutstandingTokensRouter, ServeResult, gather_request_times, serve
 from .paged_kv import (
@@ -32,6 +32,7 @@ __all__ = [
     "ContinuousBatchingRank",
     "DecodeGraph",
     "DecodeStep",
+    "FusedDecodeExecutor",
     "FusedDecoder",
     "SharedStepMetadata",
     "LeastOutstandingTokensRouter",

@@ -133,3 +133,73 @@ class FusedDecoder:
                                         self.next_ids.data_ptr(), status, _lib.stream_handle(dev)),
                    "b2pa_rows_argmax")
         return self.logits[:M], self.next_ids[:M]
+
+
+class FusedDecodeExecutor:
+    """A decode executor with the contract of the reference's
+    ``run_decode_step`` (src/serving/continuous_generate.py:198-276), for its
+    ``ContinuousBatchingScheduler`` or ``b2pa.serve``: ``executor(requests,
+    start_time_ms, event_id)`` advances every request by one greedy token and
+    returns the reference's result dict.  The step runs on ``FusedDecoder``
+    inside a ``DecodeStep`` (allocation for all layers at once, one shared
+    block table), timed like the reference's (device synchronised on both
+    sides, host work included).  The requests' KV caches must exist (their
+    prompt was prefilled).  Per-request bookkeeping follows the reference:
+    start time and batch id on first service, the new token appended, phase
+    and finish time updated, completed requests returned."""
+
+    def __init__(self, model, device, max_batch: int = 16):
+        self.model = model
+        self.device = torch.device(device)
+        self.decoder = FusedDecoder(model, max_batch=max_batch)
+        self.ids = torch.empty(max_batch, dtype=torch.int64, device=self.device)
+        self.pos = torch.empty(max_batch, dtype=torch.int64, device=self.device)
+        self.host = torch.empty(2, max_batch, dtype=torch.int64, pin_memory=True)
+        self.meta = None
+
+    @torch.no_grad()
+    def __call__(self, requests: list, start_time_ms: float, event_id: int) -> dict:
+        import time
+
+        from .paged_kv import BatchedPagedKVCache
+        from .step import DecodeStep
+
+        if not requests:
+            return {"batch_runtime_ms": 0.0, "requests_completed": []}
+        M = len(requests)
+        n_layers = len(self.decoder.layers)
+        layer_states = [[r.kv_caches[l] for r in requests] for l in range(n_layers)]
+        batches = [BatchedPagedKVCache(states=states, pool=states[0].pool) for states in layer_states]
+        torch.cuda.synchronize(self.device)
+        t0 = time.perf_counter()
+        h = self.host.numpy()
+        h[0, :M] = [r.generated_token_ids[-1] for r in requests]
+        h[1, :M] = [r.prompt_len + len(r.generated_token_ids) - 1 for r in requests]
+        self.ids[:M].copy_(self.host[0, :M], non_blocking=True)
+        self.pos[:M].copy_(self.host[1, :M], non_blocking=True)
+        step = DecodeStep(layer_states, self.meta)
+        with step:
+            _, nxt = self.decoder.step(self.ids[:M], self.pos[:M], batches)
+        self.meta = step.meta
+        next_tokens = nxt.tolist()
+        torch.cuda.synchronize(self.device)
+        elapsed_ms = (time.perf_counter() - t0) * 1000.0
+        finish_ms = start_time_ms + elapsed_ms
+        completed = []
+        for r, tok in zip(requests, next_tokens):
+            if r.start_time_ms is None:
+                r.start_time_ms = start_time_ms
+                r.batch_id = event_id
+            r.scheduler_mode = "continuous"
+            r.generated_token_ids.append(int(tok))
+            if len(r.generated_token_ids) >= r.max_new_tokens:
+                r.phase = "finished"
+                r.finish_time_ms = finish_ms
+                completed.append(r)
+            else:
+                r.phase = "decode"
+        return {"batch_runtime_ms": elapsed_ms, "requests_completed": completed, "batch_size": M,
+                "tokens_scheduled": M, "phase": "decode", "prompt_len": max(r.prompt_len for r in requests),
+                "max_new_tokens": max(r.max_new_tokens for r in requests), "prefill_tokens": 0, "decode_tokens": M,
+                "decode_kernel_tokens": M, "prefill_runtime_ms": 0.0, "decode_runtime_ms": elapsed_ms,
+                "decode_ms_per_token": elapsed_ms / M, "backend_name": "b200_paged_fused"}

@@ -40,13 +40,15 @@ from ._staging import _cudart, _rt_check
 
 class SharedStepMetadata:
     """Device buffers every layer's decode launch reads, at fixed addresses:
-    int32 ``[table (B x width) | seq_lens | start_pos | ones]`` and the int64
-    lengths ``append_batch`` returns."""
+    int32 ``[table (capacity x width) | seq_lens | start_pos | ones]`` (each
+    row segment ``capacity`` long) and the int64 lengths ``append_batch``
+    returns.  A step of B <= capacity requests uses the first B rows of each."""
 
     RING = 4  # pinned host copies: the host may plan this many steps ahead of the GPU
 
     def __init__(self, device: torch.device, B: int, width: int):
         self.device, self.B, self.width = device, B, width
+        self.capacity = B
         n = B * width + 3 * B
         self.dev = torch.empty(n, dtype=torch.int32, device=device)
         self.hosts = [torch.empty(n, dtype=torch.int32, pin_memory=True) for _ in range(self.RING)]
@@ -68,11 +70,11 @@ class SharedStepMetadata:
 
     @property
     def table(self) -> torch.Tensor:
-        return self.dev[: self.B * self.width]
+        return self.dev[: self.capacity * self.width]
 
     def _row(self, i: int) -> torch.Tensor:
-        o = self.B * self.width + i * self.B
-        return self.dev[o: o + self.B]
+        o = self.capacity * self.width + i * self.capacity
+        return self.dev[o: o + self.capacity]
 
     @property
     def seq_lens(self) -> torch.Tensor:
@@ -98,14 +100,14 @@ class SharedStepMetadata:
             _rt_check(rt.cudaEventSynchronize(self.events[i]), "cudaEventSynchronize")
         host = self.hosts[i]
         h = host.numpy()
-        B, W = self.B, self.width
+        C, W, B = self.capacity, self.width, len(tables)
         t = h[: B * W].reshape(B, W)
         t.fill(-1)
         for r, ids in enumerate(tables):
             if ids:
                 t[r, : len(ids)] = ids
-        h[B * W: B * W + B] = seq_lens
-        h[B * W + B: B * W + 2 * B] = starts
+        h[C * W: C * W + B] = seq_lens
+        h[C * W + C: C * W + C + B] = starts
         stream = _lib.stream_handle(self.device)
         _rt_check(rt.cudaMemcpyAsync(self.dev.data_ptr(), host.data_ptr(), self.nbytes, 1, stream), "cudaMemcpyAsync")
         _rt_check(rt.cudaEventRecord(self.events[i], stream), "cudaEventRecord")
@@ -117,7 +119,10 @@ class SharedStepMetadata:
             return self.workspace
         self._ws_key = key
         lib = _lib.load()
-        need = lib.b2pa_paged_decode_workspace_size(self.B, H, D, self.width, block_size, _lib.dtype_code(dtype))
+        # enough for every batch size the buffers serve (the split plan is not
+        # monotone in B)
+        need = max(lib.b2pa_paged_decode_workspace_size(b, H, D, self.width, block_size, _lib.dtype_code(dtype))
+                   for b in range(1, self.capacity + 1))
         if self.workspace is None or self.workspace.numel() < need:
             self.workspace = torch.empty(max(need, 256), dtype=torch.uint8, device=self.device)
         return self.workspace
@@ -132,7 +137,7 @@ class _StepPending:
         self.step = step
         self.k_new = k_new
         self.v_new = v_new
-        self.seq_out = step.meta.seq_out
+        self.seq_out = step.meta.seq_out[: step.B]
 
 
 class DecodeStep:
@@ -176,8 +181,11 @@ class DecodeStep:
                 raise RuntimeError("b2pa.DecodeStep.begin: a pool is already in an open step")
         device = self.pools[0].k_blocks.device
         width = self._width_needed()
-        if self.meta is None or self.meta.B != self.B or self.meta.width < width or self.meta.device != device:
-            self.meta = SharedStepMetadata(device, self.B, width + width // 2 + 16)
+        if (self.meta is None or self.meta.capacity < self.B or self.meta.width < width
+                or self.meta.device != device):
+            cap = max(self.B, self.meta.capacity if self.meta is not None else 0)
+            self.meta = SharedStepMetadata(device, cap, width + width // 2 + 16)
+        self.meta.B = self.B
         starts = reserve_lockstep(self.layer_states, self.pools)
         first = self.layer_states[0]
         self.meta.upload([s.block_ids for s in first], [s.seq_len for s in first], starts)
@@ -232,7 +240,7 @@ class DecodeStep:
         if k_new.stride(3) != 1 or v_new.stride(3) != 1:
             raise RuntimeError("b2pa.DecodeStep: k_new / v_new need a unit head_dim stride")
         cache.pool._b2pa_pending = _StepPending(self, k_new, v_new)
-        return self.meta.seq_out
+        return self.meta.seq_out[: self.B]
 
     def attend(self, q: torch.Tensor, cache, pend: _StepPending) -> torch.Tensor:
         """b2pa_paged_decode_append on the shared metadata (no host work

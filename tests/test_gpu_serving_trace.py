@@ -96,3 +96,38 @@ def test_config3_serving_trace(cuda_device):
             "virtual_gpu_ms": sum(e[3] for e in events), "wall_s": wall,
         }
     print(json.dumps(report))
+
+
+def test_config3_trace_fused_decode_executor(cuda_device):
+    """The same trace with the decode steps on b2pa.FusedDecodeExecutor (the
+    model's non-attention ops on b2pa kernels, one shared block table per
+    step) and the prompt chunks on the model: every request completes, and
+    every request's tokens equal the run with the model's own decode step."""
+    import b2pa
+
+    prev = b2pa.set_fused_append(True)
+    streams, report = {}, {"config": "BASELINE config[3] trace, one B200: decode steps on the model vs on "
+                                     "b2pa.FusedDecodeExecutor (prefill chunks on the model both ways)"}
+    try:
+        for mode in ("model_decode", "fused_decode", "model_decode", "fused_decode"):
+            model, _ = om.config0_model(om.b2pa_backend(), cuda_device)
+            ex = osv.ModelExecutors(model, cuda_device)
+            decode = b2pa.FusedDecodeExecutor(model, cuda_device, max_batch=8) if mode == "fused_decode" else ex.decode
+            warm = osv.generate_requests(8, 1000.0, 5000, [osv.WorkloadProfile("w", 256, 256, 3, 3, 1.0)], seed=1)
+            osv.ContinuousScheduler(8, 256, 1536).run(warm, ex.prefill, decode, ex.release)
+            model.pools = None
+            reqs = osv.generate_requests(200, 52.0, 5000, osv.CONFIG3_PROFILES, seed=42)
+            done, events = osv.ContinuousScheduler(8, 256, 1536).run(reqs, ex.prefill, decode, ex.release)
+            _complete(done)
+            streams[mode] = {r.request_id: list(r.generated_token_ids) for r in done}
+            ttft = [r.first_token_latency_ms for r in done]
+            dec = [e[3] for e in events if e[0] == "decode"]
+            report[mode] = {"throughput_tokens_per_s": osv.throughput_tokens_per_s(done),
+                            "ttft_p50_ms": osv.percentile(ttft, 50), "ttft_p99_ms": osv.percentile(ttft, 99),
+                            "decode_step_ms_mean": float(np.mean(dec)), "decode_events": len(dec)}
+    finally:
+        b2pa.set_fused_append(prev)
+    differ = [k for k in streams["model_decode"] if streams["model_decode"][k] != streams["fused_decode"][k]]
+    assert not differ, f"{len(differ)} requests' tokens differ: {differ[:5]}"
+    assert b2pa.read_status(cuda_device) == 0
+    print(json.dumps(report))
