@@ -805,8 +805,7 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(PfTcParams p) {
   for (int i = 0; i < PER; ++i) orow[lane + 32 * i] = from_f32<T>(o[i] / den);
 }
 
-// The fp32 variant's first step (one CTA per page and sequence, all heads):
-// copies every page that the prefill of
+// The fp32 variant's first step: copies every page that the prefill of
 // sequence b reads (pages holding keys below min(seq_len, table width)) of K
 // and of V into the workspace as fp16 hi/lo rows -- row (slot * H + h) * BS
 // + r holds hi in columns [0, D) and lo in [D, 2D), slot = b * max_pages +
@@ -843,11 +842,9 @@ struct PfSplitArgs {
 };
 
 template <int D, int BS>
-__global__ void __launch_bounds__(256) prefill_split_pages_kernel(PfSplitArgs a) {
+__global__ void __launch_bounds__(128) prefill_split_pages_kernel(PfSplitArgs a) {
   pdl_launch_dependents();  // the tensor-core kernel may launch now; it waits for this grid
-  // one CTA per (page, sequence), every head of the page: a (page, head) is
-  // only 2 x 4 KB, too little work for a CTA of its own
-  const int i = blockIdx.x, b = blockIdx.y;
+  const int i = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   int64_t kend = a.seq_lens[b];
   const int64_t cap = (int64_t)a.max_pages * BS;
   kend = kend < cap ? kend : cap;
@@ -857,11 +854,11 @@ __global__ void __launch_bounds__(256) prefill_split_pages_kernel(PfSplitArgs a)
     const int32_t raw = a.page_table[(int64_t)b * a.pt_stride + i];
     if (raw >= 0 && raw < a.num_blocks) {
       blk = raw;
-    } else if (raw >= a.num_blocks && threadIdx.x == 0) {
+    } else if (raw >= a.num_blocks && h == 0 && threadIdx.x == 0) {
       set_status(a.status, B2PA_ERR_BAD_BLOCK_ID);
     }
   }
-  if (threadIdx.x == 0) a.slots[slot] = (int32_t)(blk >= 0 ? slot : -1);
+  if (h == 0 && threadIdx.x == 0) a.slots[slot] = (int32_t)(blk >= 0 ? slot : -1);
   // positions [app_lo, app_hi) of sequence b come from k_new / v_new
   int64_t app_lo = 0, app_hi = 0;
   if (a.app_len != nullptr) {
@@ -871,22 +868,18 @@ __global__ void __launch_bounds__(256) prefill_split_pages_kernel(PfSplitArgs a)
       app_lo = a.app_start[b];
       app_hi = app_lo + len;
       if (app_lo < 0 || app_hi != (int64_t)a.seq_lens[b]) {  // not the chunk that ends the sequence
-        if (i == 0 && threadIdx.x == 0) set_status(a.status, B2PA_ERR_INVALID_ARGUMENT);
+        if (i == 0 && h == 0 && threadIdx.x == 0) set_status(a.status, B2PA_ERR_INVALID_ARGUMENT);
         app_lo = app_hi = 0;
       }
     }
-    if (a.seq_out != nullptr && i == 0 && threadIdx.x == 0) a.seq_out[b] = a.seq_lens[b];
+    if (a.seq_out != nullptr && i == 0 && h == 0 && threadIdx.x == 0) a.seq_out[b] = a.seq_lens[b];
   }
   if (blk < 0) return;
+  const int64_t src = ((blk * a.H + h) * BS) * D;
+  const int64_t dst = ((slot * a.H + h) * BS) * (2 * D);
   bool in_range = true;
-  // items: (head, row, 8-column chunk), consecutive threads on consecutive chunks of a row
-  const int per_head = BS * D / 8;
-  for (int idx = threadIdx.x; idx < a.H * per_head; idx += blockDim.x) {
-    const int h = idx / per_head;
-    const int rem = idx - h * per_head;
-    const int r = rem / (D / 8), c8 = rem - (rem / (D / 8)) * (D / 8);
-    const int64_t src = ((blk * a.H + h) * BS) * D;
-    const int64_t dst = ((slot * a.H + h) * BS) * (2 * D);
+  for (int idx = threadIdx.x; idx < BS * D / 8; idx += blockDim.x) {
+    const int r = idx / (D / 8), c8 = idx - (idx / (D / 8)) * (D / 8);
     const int64_t pos = (int64_t)i * BS + r;
     const bool fresh = pos >= app_lo && pos < app_hi;
 #pragma unroll
@@ -971,7 +964,8 @@ int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream, uint32_t epoch = 0
     if (!encode_pool_tensor_map(&tmk, sa.k_split, rows, 2 * D, BS, B2PA_DTYPE_F16) ||
         !encode_pool_tensor_map(&tmv, sa.v_split, rows, 2 * D, BS, B2PA_DTYPE_F16))
       return set_error(B2PA_ERR_CUDA, "paged_prefill: cuTensorMapEncodeTiled failed for the split pages");
-    prefill_split_pages_kernel<D, BS><<<dim3((unsigned)a.max_pages, (unsigned)a.B), 256, 0, stream>>>(sa);
+    prefill_split_pages_kernel<D, BS><<<dim3((unsigned)a.max_pages, (unsigned)a.H, (unsigned)a.B), 128, 0, stream>>>(
+        sa);
     table = sa.slots;
     pt_stride = a.max_pages;
     num_blocks = nslots;
