@@ -296,7 +296,7 @@ AttnArgs make_attn_args(const void* q, const int64_t* qs, const void* k_pool, co
                         const int32_t* cur_lens, void* out, const int64_t* os, int B, int H, int T, int D,
                         int block_size, float scale, int dtype, void* workspace, size_t workspace_bytes,
                         int32_t* status) {
-  AttnArgs a;
+  AttnArgs a = {};
   a.q = q;
   for (int i = 0; i < 4; ++i) {
     a.sq[i] = qs[i];
@@ -561,6 +561,7 @@ int b2pa_paged_prefill_append(const void* q, const int64_t q_strides[4], const v
   rc = b2pa_kv_append(k_new, new_k_strides, v_new, new_v_strides, k_pool, v_pool, pool_strides, num_blocks, page_table,
                       pt_stride, max_pages, start_pos, lengths, B, H, T, D, block_size, dtype, status, stream);
   if (rc != B2PA_OK) return rc;
+  a.after_append = 1;
   switch (dtype) {
     case B2PA_DTYPE_F32: rc = launch_paged_prefill_f32(a, s); break;
     case B2PA_DTYPE_BF16: rc = launch_paged_prefill_bf16(a, s); break;

@@ -103,6 +103,12 @@ struct AttnArgs {
   const int32_t* app_len;
   int app_vb;
   int64_t* seq_out;
+  // The kernel before the attention in the stream is b2pa's append kernel,
+  // which waits for its own predecessors before it lets dependents launch:
+  // everything but the pool pages it writes is complete when the attention
+  // starts, so the attention may set up (and read q and the table) before
+  // waiting for it.
+  int after_append;
 };
 
 int launch_kv_append(const AppendArgs& a, cudaStream_t stream);

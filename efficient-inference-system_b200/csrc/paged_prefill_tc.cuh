@@ -77,6 +77,10 @@ struct PfTcParams {
   // Marking with the call's number needs no reset between calls.
   uint32_t* range_flag;
   uint32_t epoch;
+  // 1: the kernel before this one is b2pa's append kernel (see
+  // AttnArgs::after_append): only the K/V producers wait for it, before
+  // their first page copy; set-up, q and the block table go ahead.
+  int early;
 };
 
 // Inputs of the fp32 variant must stay below 2^15 in magnitude (fp16 holds
@@ -264,8 +268,9 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // Launched programmatically after the kernel before it (the KV append of
   // the step, or the fp32 variant's pre-pass): wait for its results before
-  // reading anything; let the next kernel launch behind this grid.
-  pdl_wait();
+  // reading anything (after the append kernel, only before reading pool
+  // pages: see PfTcParams::early); let the next kernel launch behind this grid.
+  if (!p.early) pdl_wait();
   pdl_launch_dependents();
   if constexpr (SPLIT) {
     // an input out of the split's range was seen (pre-pass or another CTA):
@@ -332,6 +337,7 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
     } else {
       named_bar_sync(1, C::THREADS);  // barriers initialised
     }
+    if (p.early) pdl_wait();  // the append kernel's rows are in the pages about to be copied
     unsigned char* ring = is_k ? sK : sV;
     const CUtensorMap* tmap = is_k ? &tm_k : &tm_v;
     uint64_t* full = is_k ? k_full : v_full;
@@ -1002,6 +1008,7 @@ int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream, uint32_t epoch = 0
   p.part_ml = nullptr;
   p.range_flag = range_flag;
   p.epoch = epoch;
+  p.early = (!SPLIT && a.after_append) ? 1 : 0;
   if (plan.nsplit_max > 1) {
     p.part_ml = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + plan.off_part_ml);
     p.part_o = reinterpret_cast<float*>(static_cast<char*>(a.workspace) + plan.off_part_o);
