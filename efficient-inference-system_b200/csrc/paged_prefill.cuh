@@ -73,23 +73,17 @@ struct PrefillSmem {
   static constexpr size_t BYTES = 4ull * (Q_FLOATS + K_FLOATS + V_FLOATS + P_FLOATS + kPfTK);
 };
 
+// One (32 query rows, head, sequence) tile of the general kernel.
 template <typename T, int D, int BS>
-__global__ void __launch_bounds__(kPfThreads) paged_prefill_simt_kernel(PrefillParams p) {
+__device__ __forceinline__ void paged_prefill_simt_tile(const PrefillParams& p, int tile, int h, int b, float* psm) {
   using S = PrefillSmem<D>;
-  if (p.run_if != nullptr) {  // a backup launch (programmatic): nothing to redo unless the flag says so
-    pdl_wait();
-    if (*p.run_if != p.run_epoch) return;
-  }
-  extern __shared__ __align__(16) float psm[];
   float* Qs = psm;
   float* Ks = Qs + S::Q_FLOATS;
   float* Vs = Ks + S::K_FLOATS;
   float* Ps = Vs + S::V_FLOATS;
   int* Kok = reinterpret_cast<int*>(Ps + S::P_FLOATS);  // key row came from a real page
 
-  const int t0 = blockIdx.x * kPfTQ;
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
+  const int t0 = tile * kPfTQ;
   const int tid = threadIdx.x;
   if (t0 >= p.T) return;
 
@@ -214,6 +208,27 @@ __global__ void __launch_bounds__(kPfThreads) paged_prefill_simt_kernel(PrefillP
   }
 }
 
+template <typename T, int D, int BS>
+__global__ void __launch_bounds__(kPfThreads) paged_prefill_simt_kernel(PrefillParams p) {
+  extern __shared__ __align__(16) float psm[];
+  if (p.run_if != nullptr) {
+    // A backup launch (programmatic): nothing to redo unless the flag says
+    // so.  It runs as a persistent grid (one CTA per SM) over the tiles, so
+    // that the usual case -- check the flag, exit -- retires few CTAs.
+    pdl_wait();
+    if (*p.run_if != p.run_epoch) return;
+    const int nx = (p.T + kPfTQ - 1) / kPfTQ;
+    const int64_t total = (int64_t)nx * p.H * p.B;
+    for (int64_t it = blockIdx.x; it < total; it += gridDim.x) {
+      __syncthreads();  // the previous tile's threads are done with shared memory
+      paged_prefill_simt_tile<T, D, BS>(p, (int)(it % nx), (int)((it / nx) % p.H), (int)(it / ((int64_t)nx * p.H)),
+                                        psm);
+    }
+    return;
+  }
+  paged_prefill_simt_tile<T, D, BS>(p, blockIdx.x, blockIdx.y, blockIdx.z, psm);
+}
+
 // run_if / run_epoch: a backup launch, which does nothing unless *run_if ==
 // run_epoch (the fp16-split tensor-core kernel met an input out of range).
 template <typename T, int D, int BS>
@@ -256,7 +271,9 @@ int launch_prefill_simt(const AttnArgs& a, cudaStream_t stream, const uint32_t* 
   cudaError_t e;
   dim3 grid((a.T + kPfTQ - 1) / kPfTQ, a.H, a.B);
   if (run_if != nullptr) {
-    e = launch_pdl(kern, grid, dim3(kPfThreads), smem, stream, p);
+    const int64_t total = (int64_t)grid.x * grid.y * grid.z;
+    const int64_t sms = device_sm_count();
+    e = launch_pdl(kern, dim3((unsigned)(total < sms ? total : sms)), dim3(kPfThreads), smem, stream, p);
     if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill launch: %s", cudaGetErrorString(e));
   } else {
     kern<<<grid, kPfThreads, smem, stream>>>(p);
