@@ -261,6 +261,13 @@ extern "C" int b2pa_rows_linear(const float* x, int64_t x_row_stride, int M, int
   if (!aligned16(x) || !aligned16(weight) || x_row_stride % 4 || x_row_stride < K || y_row_stride < N ||
       (ln_weight && !aligned16(ln_weight)) || (ln_bias && !aligned16(ln_bias)))
     return set_error(B2PA_ERR_UNSUPPORTED, "rows_linear: x, weight and LayerNorm vectors need 16-byte rows");
+  {
+    // every CTA reads all of x while others already write y: they must not overlap
+    const uintptr_t x0 = reinterpret_cast<uintptr_t>(x), y0 = reinterpret_cast<uintptr_t>(y);
+    const uintptr_t x1 = x0 + 4 * (uintptr_t)((int64_t)(M - 1) * x_row_stride + K);
+    const uintptr_t y1 = y0 + 4 * (uintptr_t)((int64_t)(M - 1) * y_row_stride + N);
+    if (x0 < y1 && y0 < x1) return set_error(B2PA_ERR_INVALID_ARGUMENT, "rows_linear: y overlaps x");
+  }
   RowsLinearArgs a;
   a.x = x;
   a.xs = x_row_stride;

@@ -184,3 +184,24 @@ def test_missing_library_raises(monkeypatch, tmp_path):
     monkeypatch.setenv("B2PA_LIB", str(tmp_path / "nope.so"))
     with pytest.raises(RuntimeError, match="not found"):
         _lib.load()
+
+
+def test_row_ops_argument_validation(lib):
+    """The decode-step row operations refuse bad arguments before launching
+    (addresses are never dereferenced here)."""
+    def linear(M=2, K=64, N=32, x=4096, xs=64, w=1 << 20, y=1 << 22, ys=32, act=0, ln=None):
+        return lib.b2pa_rows_linear(x, xs, M, K, ln, None, 1e-5, w, None, N, act, y, ys, 0, None, None)
+
+    assert linear(M=17) == -1                      # more than 16 rows
+    assert linear(K=62, xs=64) == -2               # K not a multiple of 4
+    assert linear(xs=60) == -2                     # row stride below K
+    assert linear(x=4100) == -2                    # x not 16-byte aligned
+    assert linear(act=3) == -2                     # unknown activation
+    assert linear(ln=4104) == -2                   # LayerNorm weight not 16-byte aligned
+    assert linear(y=4096 + 256) == -1              # y overlaps x
+    assert "overlaps" in _lib.last_error()
+    assert linear(M=0) == 0                        # nothing to do
+    assert lib.b2pa_rows_embed(None, None, 1, 16, 10, 16, 10, 64, 16, 64, None, None) == -1
+    assert lib.b2pa_rows_embed(16, 16, 1, 16, 10, 16, 10, 62, 16, 64, None, None) == -2
+    assert lib.b2pa_rows_argmax(16, 10, 1, 20, 16, None, None) == -1  # row stride below N
+    assert lib.b2pa_rows_argmax(16, 20, 0, 20, 16, None, None) == 0
