@@ -1029,6 +1029,85 @@ def main_secondary(args) -> int:
     return 0
 
 
+def measure_decode_step(torch, dev, steps: int = 120, prompt: int = 128) -> dict:
+    """config[0]'s decode step on b2pa kernels: b2pa.FusedDecoder (row kernels +
+    the fused append/decode) replayed as a CUDA graph (b2pa.DecodeGraph), batch
+    1, after a 128-token prompt.  The weights are seeded random values in a
+    parameter container with the config[0] model's shapes under the
+    reference's module names (vocab 5000, d_model 512, 8 heads, 6 layers,
+    d_ff 2048); the prompt's K/V rows are random, appended to every layer's
+    pool through BatchedPagedKVCache.append_batch.  Tokens stay on the device;
+    one synchronisation at the end.  (Correctness of this path is checked by
+    the GPU tests against the reference's tokens.)"""
+    import torch.nn as nn
+
+    import b2pa
+
+    V, d, Hh, L, dff = 5000, 512, 8, 6, 2048
+
+    class _Attn(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.num_heads = Hh
+            self.q_proj, self.k_proj, self.v_proj, self.out_proj = (nn.Linear(d, d) for _ in range(4))
+
+    class _Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.ln1, self.attn, self.ln2 = nn.LayerNorm(d), _Attn(), nn.LayerNorm(d)
+            self.mlp = nn.Sequential(nn.Linear(d, dff), nn.GELU(), nn.Linear(dff, d))
+
+    class _Model(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.token_emb, self.pos_emb = nn.Embedding(V, d), nn.Embedding(1024, d)
+            self.blocks = nn.ModuleList(_Block() for _ in range(L))
+            self.ln_f, self.lm_head = nn.LayerNorm(d), nn.Linear(d, V, bias=False)
+
+    torch.manual_seed(SEED)
+    model = _Model().to(dev).eval()
+    gen = torch.Generator(device=dev).manual_seed(SEED)
+    states = []
+    for _ in range(L):
+        pool = b2pa.LayerBlockPool(block_size=16, initial_blocks=64, growth_factor=2.0)
+        st = b2pa.PagedKVCacheState(pool=pool)
+        kv = torch.randn(2, 1, Hh, prompt, d // Hh, generator=gen, device=dev)
+        b2pa.BatchedPagedKVCache([st], pool=pool).append_batch(kv[0], kv[1], prompt)
+        states.append(st)
+    layer_states = [[st] for st in states]
+    batches = [b2pa.BatchedPagedKVCache([st], pool=st.pool) for st in states]
+    dec = b2pa.FusedDecoder(model, max_batch=1)
+    ids = torch.zeros(1, dtype=torch.int64, device=dev)
+    pos = torch.zeros(1, dtype=torch.int64, device=dev)
+    toks = torch.empty(steps, dtype=torch.int64, device=dev)
+    graph = b2pa.DecodeGraph(lambda: dec.step(ids, pos, batches)[1])
+    with torch.no_grad():
+        for s in range(3):  # warm-up and capture
+            pos.fill_(prompt + s)
+            ids.copy_(graph(layer_states))
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        for s in range(steps):
+            pos.fill_(prompt + 3 + s)
+            nx = graph(layer_states)
+            toks[s] = nx[0]
+            ids.copy_(nx)
+        torch.cuda.synchronize(dev)
+        secs = time.perf_counter() - t0
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(20):  # replays rewrite the last step's rows with the same values
+            graph.graph.replay()
+        b.record()
+        torch.cuda.synchronize(dev)
+    weights = sum(p.numel() for n, p in model.named_parameters() if "emb" not in n) * 4
+    return {"tokens_per_s": steps / secs, "ms_per_token": secs / steps * 1e3,
+            "device_us_per_step": a.elapsed_time(b) / 20 * 1e3, "graph_captures": graph.captures,
+            "weight_bytes_per_step": weights,
+            "what": "config[0] decode step (batch 1, 128-token prompt, 6 layers, fp32) on b2pa.FusedDecoder as a "
+                    "CUDA graph; seeded random weights with the config[0] shapes"}
+
+
 def secondary_summary(args) -> dict:
     """The secondary kernels timed inside the main bench run (one GPU):
     config[2] chunked prefill bf16 and fp32, the same with 4096-token
@@ -1054,6 +1133,7 @@ def secondary_summary(args) -> dict:
         line = measure_secondary(torch, lib, _lib, dev, workload, dtype, max(args.steps, 10), args.warmup,
                                  None, plen)
         out[name] = {k: line[k] for k in keep if k in line}
+    out["decode_step_config0"] = measure_decode_step(torch, dev)
     out["timing"] = ("CUDA events; L2 flushed before every call; attention_ms: one CUDA-graph replay of the call "
                      "(includes ~6 us of replay launch overhead); attention_ms_in_graph: per call inside a graph of "
                      "10 flushed calls minus the flushes; step times: eager calls")
