@@ -8,7 +8,10 @@ node has GPUs for; needs at least two GPUs.
 Checks: every request completes on exactly one rank with its token budget,
 and every request's token stream is identical to the one-GPU run.  Prints
 tokens/s and p50/p99 time to first token per N (virtual clock advanced by
-measured GPU time, as the reference's scheduler does)."""
+measured GPU time, as the reference's scheduler does).  A second, saturated
+run -- the same requests all arriving at once, decode steps on
+b2pa.FusedDecodeExecutor -- shows how throughput scales with N when arrivals
+do not bound it; its tokens must equal the first run's too."""
 from __future__ import annotations
 
 import json
@@ -60,16 +63,37 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
         assert all(r.num_generated_tokens == r.max_new_tokens for r in res.completed)
         assert b2pa.read_status(dev) == 0
         b2pa.set_fused_append(prev)
+        # saturated: the same request mix all arriving at once, decode steps on b2pa.FusedDecodeExecutor
+        prev = b2pa.set_fused_append(True)
+        model_s, _ = om.config0_model(om.b2pa_backend(), dev)
+        ex_s = osv.ModelExecutors(model_s, dev)
+        fused = b2pa.FusedDecodeExecutor(model_s, dev, max_batch=8)
+        osv.ContinuousScheduler(8, 256, 1536).run(
+            osv.generate_requests(8, 1000.0, 5000, [osv.WorkloadProfile("w", 256, 256, 3, 3, 1.0)], seed=1),
+            ex_s.prefill, fused, ex_s.release)
+        model_s.pools = None
+        sat = osv.generate_requests(200, 52.0, 5000, osv.CONFIG3_PROFILES, seed=42)
+        for r in sat:
+            r.arrival_time_ms = 0.0
+        res_s = b2pa.serve(sat, ex_s.prefill, fused, ex_s.release, max_batch_size=8, prefill_chunk_size=256,
+                           max_tokens_per_iteration=1536, device=dev)
+        times_s = b2pa.gather_request_times(res_s.completed)
+        assert b2pa.read_status(dev) == 0
+        b2pa.set_fused_append(prev)
         if rank == 0:
             budget = {r.request_id: r.max_new_tokens for r in reqs}
-            ttft = [ft - a for _, a, ft, _ in times]
-            makespan = max(f for *_, f in times) - min(a for _, a, _, _ in times)
-            out = {"n_gpus": world, "completed": len(times),
-                   "per_rank_requests": [sum(1 for o in res.owner.values() if o == w) for w in range(world)],
-                   "throughput_tokens_per_s": sum(budget.values()) / (makespan / 1000.0),
-                   "ttft_p50_ms": osv.percentile(ttft, 50), "ttft_p99_ms": osv.percentile(ttft, 99),
-                   "makespan_ms": makespan, "iterations": res.iterations,
-                   "streams": {str(k): v for k, v in res.token_streams.items()}}
+
+            def summary(rs, tm):
+                ttft = [ft - a for _, a, ft, _ in tm]
+                makespan = max(f for *_, f in tm) - min(a for _, a, _, _ in tm)
+                return {"completed": len(tm),
+                        "per_rank_requests": [sum(1 for o in rs.owner.values() if o == w) for w in range(world)],
+                        "throughput_tokens_per_s": sum(budget.values()) / (makespan / 1000.0),
+                        "ttft_p50_ms": osv.percentile(ttft, 50), "ttft_p99_ms": osv.percentile(ttft, 99),
+                        "makespan_ms": makespan, "iterations": rs.iterations,
+                        "streams": {str(k): v for k, v in rs.token_streams.items()}}
+
+            out = {"n_gpus": world, **summary(res, times), "saturated_fused_decode": summary(res_s, times_s)}
             with open(os.path.join(out_dir, f"serve_n{world}.json"), "w") as f:
                 json.dump(out, f)
     finally:
@@ -87,16 +111,24 @@ def test_config3_trace_on_several_gpus(tmp_path):
     n_dev = torch.cuda.device_count()
     if n_dev < 2:
         pytest.skip("needs at least two GPUs")
+    def brief(res):
+        out = {k: v for k, v in res.items() if k not in ("streams", "saturated_fused_decode")}
+        out["saturated_fused_decode"] = {k: v for k, v in res["saturated_fused_decode"].items() if k != "streams"}
+        return out
+
     one = _run(1, str(tmp_path))
-    assert one["completed"] == 200
-    report = [{k: v for k, v in one.items() if k != "streams"}]
+    assert one["completed"] == 200 and one["saturated_fused_decode"]["completed"] == 200
+    # the saturated run's decode steps are on the fused executor: same tokens as the model's own steps
+    assert one["saturated_fused_decode"]["streams"] == one["streams"]
+    report = [brief(one)]
     for world in (2, 4, 8):
         if world > n_dev:
             break
         res = _run(world, str(tmp_path))
-        assert res["completed"] == 200
-        assert sum(res["per_rank_requests"]) == 200 and min(res["per_rank_requests"]) > 0
-        differ = [k for k in one["streams"] if one["streams"][k] != res["streams"][k]]
-        assert not differ, f"{len(differ)} requests' token streams differ from the one-GPU run: {differ[:5]}"
-        report.append({k: v for k, v in res.items() if k != "streams"})
+        for run in (res, res["saturated_fused_decode"]):
+            assert run["completed"] == 200
+            assert sum(run["per_rank_requests"]) == 200 and min(run["per_rank_requests"]) > 0
+            differ = [k for k in one["streams"] if one["streams"][k] != run["streams"][k]]
+            assert not differ, f"{len(differ)} requests' token streams differ from the one-GPU run: {differ[:5]}"
+        report.append(brief(res))
     print(json.dumps(report))
