@@ -16,18 +16,19 @@ of a ``torch.distributed`` group over the requests routed to the rank:
   tokens not yet generated), ties to the lowest rank.  Every rank evaluates
   it on the same data, so all ranks make the same decisions without a
   message;
-* ``serve`` -- the lockstep loop.  Per iteration each rank runs its own
-  scheduler (its requests' attention and KV appends touch only its own
+* ``serve`` -- the loop.  Per iteration each rank runs one iteration of its
+  own scheduler (its requests' attention and KV appends touch only its own
   pools: no collective on that path), then the ranks exchange, in two
   collectives, the token ids they sampled and a small vector of statistics
-  (iteration time, outstanding tokens, completed requests) -- the only
-  traffic between GPUs.  The shared virtual clock advances by the slowest
-  rank's iteration time, as the reference's advances by measured runtime.
+  (virtual clock, outstanding tokens, completed requests) -- the only
+  traffic between GPUs.  Each rank keeps its own virtual clock, advanced by
+  its measured runtime as the reference's is (the ranks run in parallel);
+  a request is routed once every rank's clock has passed its arrival, and a
+  rank with nothing to do moves its clock on to the next arrival.
 
 With one rank ``serve`` reproduces the reference's ``run`` event for event
 (the router hands every request to rank 0 up front and the rank's own
-arrival rules apply).  With more, requests that arrive during an iteration
-are routed at the next exchange.
+arrival rules apply).
 
 Requests and executors are the reference's (``InferenceRequest``,
 ``run_prefill_chunk`` / ``run_decode_step`` from src/serving/
@@ -236,22 +237,28 @@ def serve(requests: list, prefill_executor, decode_executor, release=None, *, ma
     if device is None:
         device = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
     cap = 4 * max_batch_size  # tokens one rank can emit in one iteration (at most 2 per active slot)
+    NS = 5                    # statistics per rank: clock, outstanding tokens, completed, tokens emitted, active
     tok_out = torch.empty(world * cap * 2, dtype=torch.int64, device=device)
-    stat_out = torch.empty(world * 4, dtype=torch.float64, device=device)
-    nxt, now, total_done = 0, 0.0, 0
-    all_idle = True
+    stat_out = torch.empty(world * NS, dtype=torch.float64, device=device)
+    nxt, clock, total_done = 0, 0.0, 0
+    clocks = np.zeros(world)
     for r in requests:
         result.token_streams[r.request_id] = []
     while total_done < len(requests):
-        if all_idle and nxt < len(requests):
-            now = max(now, requests[nxt].arrival_time_ms)
-        while nxt < len(requests) and requests[nxt].arrival_time_ms <= now:
+        # Route the requests every rank's clock has passed (all ranks see the
+        # same clocks from the last exchange, so all route alike).
+        horizon = float(clocks.min())
+        while nxt < len(requests) and requests[nxt].arrival_time_ms <= horizon:
             owner = router.route(requests[nxt])
             result.owner[requests[nxt].request_id] = owner
             if owner == rank:
                 sched.assign(requests[nxt])
             nxt += 1
-        end = sched.iterate(now, prefill_executor, decode_executor, release) if sched.has_work() else now
+        if sched.has_work():
+            clock = sched.iterate(clock, prefill_executor, decode_executor, release)
+        elif nxt < len(requests):
+            # idle: move on to the next arrival, so that routing can proceed
+            clock = max(clock, requests[nxt].arrival_time_ms)
         new = sched.take_new_tokens()
         if len(new) > cap:
             raise RuntimeError(f"b2pa.serve: {len(new)} tokens in one iteration exceed the exchange size {cap}")
@@ -260,21 +267,25 @@ def serve(requests: list, prefill_executor, decode_executor, release=None, *, ma
             mine[: len(new)] = torch.tensor(new, dtype=torch.int64)
         # the two exchanges of an iteration: sampled tokens, then statistics
         dist.all_gather_into_tensor(tok_out, mine.reshape(-1).to(device), group=group)
-        stats = torch.tensor([end - now, float(sched.outstanding_tokens()), float(len(sched.completed)),
-                              float(len(new))], dtype=torch.float64)
+        stats = torch.tensor([clock, float(sched.outstanding_tokens()), float(len(sched.completed)), float(len(new)),
+                              float(sched.has_work())], dtype=torch.float64)
         dist.all_gather_into_tensor(stat_out, stats.to(device), group=group)
         toks = tok_out.view(world, cap, 2).cpu().numpy()
-        st = stat_out.view(world, 4).cpu().numpy()
+        st = stat_out.view(world, NS).cpu().numpy()
         for w in range(world):
             for rid, tok in toks[w, : int(st[w, 3])]:
                 result.token_streams[int(rid)].append(int(tok))
-        now += float(st[:, 0].max())
+        clocks = st[:, 0].copy()
+        # a rank with nothing to do does not hold routing back
+        busy = st[:, 4] > 0
+        if nxt < len(requests) and not busy.all():
+            clocks[~busy] = np.maximum(clocks[~busy], min(requests[nxt].arrival_time_ms, clocks[busy].max())
+                                       if busy.any() else requests[nxt].arrival_time_ms)
         router.sync(st[:, 1])
         total_done = int(st[:, 2].sum())
-        all_idle = not st[:, 1].any()
         result.iterations += 1
     sched.completed.sort(key=lambda r: r.request_id)
-    result.makespan_ms = now
+    result.makespan_ms = float(clocks.max())
     return result
 
 
