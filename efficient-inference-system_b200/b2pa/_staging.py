@@ -60,6 +60,8 @@ def _cudart():
         lib.cudaEventRecord.restype = ctypes.c_int
         lib.cudaEventSynchronize.argtypes = [ctypes.c_void_p]
         lib.cudaEventSynchronize.restype = ctypes.c_int
+        lib.cudaEventDestroy.argtypes = [ctypes.c_void_p]
+        lib.cudaEventDestroy.restype = ctypes.c_int
         _rt = lib
     return _rt
 

@@ -68,6 +68,15 @@ class SharedStepMetadata:
         self.workspace: torch.Tensor | None = None
         self._ws_key = None
 
+    def __del__(self):
+        # the ring's events; the CUDA runtime may already be gone at exit
+        try:
+            rt = _cudart()
+            for ev in getattr(self, "events", []):
+                rt.cudaEventDestroy(ev)
+        except Exception:  # noqa: BLE001 -- nothing to clean up with then
+            pass
+
     @property
     def table(self) -> torch.Tensor:
         return self.dev[: self.capacity * self.width]

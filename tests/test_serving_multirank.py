@@ -108,3 +108,40 @@ def test_two_gloo_ranks_serve_the_trace(tmp_path):
     one = b2pa.serve(_trace(), osv.fake_prefill_executor, osv.fake_decode_executor, max_batch_size=8,
                      prefill_chunk_size=256, max_tokens_per_iteration=1536)
     assert outs[0]["makespan"] <= one.makespan_ms
+
+
+def _saturated_worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    try:
+        reqs = _trace()
+        for r in reqs:
+            r.arrival_time_ms = 0.0
+        res = b2pa.serve(reqs, osv.fake_prefill_executor, osv.fake_decode_executor, max_batch_size=8,
+                         prefill_chunk_size=256, max_tokens_per_iteration=1536, device=torch.device("cpu"))
+        if rank == 0:
+            np.save(os.path.join(out_dir, "sat.npy"), np.array([{"makespan": res.makespan_ms,
+                                                                 "streams": res.token_streams}], dtype=object),
+                    allow_pickle=True)
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_ranks_share_a_saturated_load(tmp_path):
+    """Every request arriving at once: each rank serves its share on its own
+    clock, so two ranks finish in well under one rank's time (a single shared
+    clock advanced by the slower rank's iteration did not)."""
+    reqs = _trace()
+    for r in reqs:
+        r.arrival_time_ms = 0.0
+    one = b2pa.serve(reqs, osv.fake_prefill_executor, osv.fake_decode_executor, max_batch_size=8,
+                     prefill_chunk_size=256, max_tokens_per_iteration=1536)
+    mp.spawn(_saturated_worker, args=(2, _free_port(), str(tmp_path)), nprocs=2, join=True)
+    two = np.load(tmp_path / "sat.npy", allow_pickle=True)[0]
+    assert two["makespan"] < 0.6 * one.makespan_ms
+    assert two["streams"] == one.token_streams
