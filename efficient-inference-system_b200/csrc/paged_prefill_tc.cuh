@@ -81,6 +81,11 @@ struct PfTcParams {
   // AttnArgs::after_append): only the K/V producers wait for it, before
   // their first page copy; set-up, q and the block table go ahead.
   int early;
+  // 1: Q is loaded by one TMA box per 64 columns (16-bit q whose layout the
+  // tensor map takes); q_dim[0..2]: the map dimension of t, h, b.  0: the
+  // softmax threads load it.
+  int q_tma;
+  int q_dim[3];
 };
 
 // Inputs of the fp32 variant must stay below 2^15 in magnitude (fp16 holds
@@ -148,8 +153,9 @@ struct PfTcCfg {
   static constexpr int OFF_V = OFF_K + STAGES * KV_BYTES;
   static constexpr int OFF_P = OFF_V + STAGES * KV_BYTES;
   static constexpr int OFF_BAR = OFF_P + NSLOT * P_BYTES;
-  // k_full, k_empty, v_full, v_empty [STAGES each], s_full, p_full, p_free [NSLOT each], o_full[NG], o_final
-  static constexpr int N_BARS = 4 * STAGES + 3 * NSLOT + NG + 1;
+  // k_full, k_empty, v_full, v_empty [STAGES each], s_full, p_full, p_free [NSLOT each], o_full[NG], o_final,
+  // q_full
+  static constexpr int N_BARS = 4 * STAGES + 3 * NSLOT + NG + 2;
   static constexpr int OFF_MISC = OFF_BAR + 8 * N_BARS;  // TMEM base, abort flag
   static constexpr int OFF_ML = OFF_MISC + 16;           // per-group (m, l) of every row, for the merge
   static constexpr int OFF_BLK = OFF_ML + (NG > 1 ? 2 * NG * BM * 4 : 0);  // int32 block ids of the CTA's pages
@@ -239,7 +245,7 @@ __device__ __forceinline__ void split_f16x8(const float (&f)[8], uint4& hi, uint
 template <typename T, int D, int BS>
 __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
     paged_prefill_tc_kernel(const __grid_constant__ CUtensorMap tm_k, const __grid_constant__ CUtensorMap tm_v,
-                            PfTcParams p) {
+                            const __grid_constant__ CUtensorMap tm_q, PfTcParams p) {
   constexpr bool SPLIT = kPfSplit<T>;
   using C = PfTcCfg<D, BS, SPLIT>;
   constexpr int NG = C::NG, NSLOT = C::NSLOT;
@@ -260,6 +266,7 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
   uint64_t* p_free = p_full + NSLOT;        // [NSLOT]: P.V(j) done, P buffer free
   uint64_t* o_full = p_free + NSLOT;        // [NG]: one phase per P.V MMA of the group
   uint64_t* o_final = o_full + NG;          // one phase: every P.V of the CTA done
+  uint64_t* q_full = o_final + 1;           // one phase: Q landed (TMA load of Q only)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_MISC);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::OFF_MISC + 4);
   float* sML = reinterpret_cast<float*>(smem + C::OFF_ML);
@@ -298,6 +305,43 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
     if (warp != C::QK_WARP && warp != C::PV_WARP && pg0 + i < p.max_pages) blk_pre = pt_row[pg0 + i];
   }
 
+  // The K producer's lane 0 initialises the barriers at once and, when no
+  // CTA of the launch can leave early (no key-range split), issues the TMA
+  // load of Q before the sequence length is even known; otherwise once the
+  // CTA is known to stay.  The QK issuer waits for it in every case.
+  const bool q_first = p.q_tma && p.nsplit_max == 1;
+  auto issue_q = [&]() {
+    mbar_arrive_expect_tx(q_full, (uint32_t)C::Q_BYTES);
+    auto coord = [&](int d) { return p.q_dim[0] == d ? t0 : (p.q_dim[1] == d ? h : b); };
+#pragma unroll
+    for (int kb = 0; kb < C::KB; ++kb)
+      tc::tma_load_4d(sQ + kb * (C::BM * 128), &tm_q, kb * 64, coord(1), coord(2), coord(3), q_full);
+  };
+  if (warp == C::K_WARP && lane == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+    }
+    for (int i = 0; i < NSLOT; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&p_free[i], 1);
+    }
+    for (int g = 0; g < NG; ++g) mbar_init(&o_full[g], 1);
+    mbar_init(o_final, 1);
+    mbar_init(q_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tc::prefetch_tmap(&tm_k);
+    tc::prefetch_tmap(&tm_v);
+    if (p.q_tma) {
+      tc::prefetch_tmap(&tm_q);
+      if (q_first) issue_q();
+    }
+  }
+
   const int64_t L = p.seq_lens[b];
   const int64_t past = L - (int64_t)p.cur_lens[b];
   const int64_t cap = (int64_t)p.max_pages * BS;
@@ -314,23 +358,7 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
     if (is_k) {
       if (lane == 0) {
         if (L > cap) set_status(p.status, B2PA_ERR_BAD_BLOCK_ID);
-        for (int s = 0; s < C::STAGES; ++s) {
-          mbar_init(&k_full[s], 1);
-          mbar_init(&k_empty[s], 1);
-          mbar_init(&v_full[s], 1);
-          mbar_init(&v_empty[s], 1);
-        }
-        for (int i = 0; i < NSLOT; ++i) {
-          mbar_init(&s_full[i], 1);
-          mbar_init(&p_full[i], 4);
-          mbar_init(&p_free[i], 1);
-        }
-        for (int g = 0; g < NG; ++g) mbar_init(&o_full[g], 1);
-        mbar_init(o_final, 1);
-        *abort_flag = 0;
-        fence_mbar_init();
-        tc::prefetch_tmap(&tm_k);
-        tc::prefetch_tmap(&tm_v);
+        if (p.q_tma && !q_first) issue_q();
       }
       __syncwarp();
       named_bar_arrive(1, C::THREADS);
@@ -425,7 +453,10 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
     const uint64_t dV = tc::smem_desc(smem_u32(sV), C::BN * 128, 1024);
     const uint64_t dP = tc::smem_desc(smem_u32(sP), 16, 1024);
     if (lane == 0 && is_qk) {
-      for (int j = 0; j < ntiles; ++j) {
+      // Q by TMA: wait for it even without tiles, so that no copy is still
+      // landing when the CTA exits.
+      const bool q_ok = !p.q_tma || lane_wait(q_full, 0u, p.status, abort_flag);
+      for (int j = 0; q_ok && j < ntiles; ++j) {
         const int st = j % C::STAGES, slot = j % NSLOT;
         if (!lane_wait(&k_full[st], (uint32_t)(j / C::STAGES) & 1u, p.status, abort_flag)) break;
         if (j >= NSLOT && !lane_wait(&p_full[slot], (uint32_t)(j / NSLOT - 1) & 1u, p.status, abort_flag)) break;
@@ -484,7 +515,9 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
     const int r = tid & 127;     // query row (TMEM lane) of this thread
     const int t = t0 + r;
     // Q rows -> 128B-swizzled K-major tile, zeros past T; consecutive
-    // threads read consecutive 16-byte pieces of a row.
+    // threads read consecutive 16-byte pieces of a row (unless the TMA load
+    // of Q, issued at kernel entry, brings it).
+    if (!p.q_tma) {
 #pragma unroll
     for (int it = 0; it < C::BM * D / 8 / C::SOFTMAX_THREADS; ++it) {
       const int c = tid + it * C::SOFTMAX_THREADS;
@@ -517,6 +550,7 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
                                               (int64_t)h * p.sq_h + (int64_t)qt * p.sq_t + qc * 8);
         *reinterpret_cast<uint4*>(sQ + off) = v;
       }
+    }
     }
     tc::fence_proxy_async_smem();
     tc::fence_before_sync();
@@ -921,6 +955,8 @@ __global__ void __launch_bounds__(128) prefill_split_pages_kernel(PfSplitArgs a)
 
 // ----------------------------------------------------------------- host ---
 bool encode_pool_tensor_map(CUtensorMap* map, const void* pool, int64_t rows, int D, int block_size, int dtype);
+bool encode_q_tensor_map(CUtensorMap* map, const void* q, int B, int H, int T, int D, const int64_t sq[3], int dtype,
+                         int dim_of[3]);
 
 // epoch: the fp32 variant's number of this call (marks the range flag).
 template <typename T, int D, int BS>
@@ -1024,7 +1060,19 @@ int launch_prefill_tc(const AttnArgs& a, cudaStream_t stream, uint32_t epoch = 0
   if (rc_attr != B2PA_OK) return rc_attr;
   cudaError_t e;
   dim3 grid(((a.T + C::BM - 1) / C::BM) * plan.nsplit_max, a.H, a.B);
-  e = launch_pdl(kern, grid, dim3(C::THREADS), smem, stream, tmk, tmv, p);
+  // 16-bit q: a tensor map for its TMA load (q layouts the driver refuses
+  // are loaded by the softmax threads).
+  CUtensorMap tmq = tmk;
+  p.q_tma = 0;
+  p.q_dim[0] = 1;
+  p.q_dim[1] = 2;
+  p.q_dim[2] = 3;
+  if (!SPLIT) {
+    const int64_t sq[3] = {a.sq[0], a.sq[1], a.sq[2]};
+    p.q_tma = encode_q_tensor_map(&tmq, a.q, a.B, a.H, a.T, a.D, sq, a.dtype, p.q_dim) ? 1 : 0;
+    if (!p.q_tma) tmq = tmk;  // not read
+  }
+  e = launch_pdl(kern, grid, dim3(C::THREADS), smem, stream, tmk, tmv, tmq, p);
   if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_prefill_tc launch: %s", cudaGetErrorString(e));
   if (plan.nsplit_max > 1) {
     const int64_t rows = (int64_t)a.B * a.H * a.T;

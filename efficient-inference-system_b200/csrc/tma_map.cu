@@ -75,6 +75,44 @@ bool encode_pool_tensor_map(CUtensorMap* map, const void* pool, int64_t rows, in
   return true;
 }
 
+// q [B, H, T, D] (element strides sq = {b, h, t}, unit D stride) as a 4-d
+// tensor {D, x1, x2, x3}: the outer three are t, h, b ordered by stride, so
+// the usual layouts ([B, H, T, D], or the [B, T, H, D] view the model's head
+// split makes) are packed maps.  One box is 64 columns (128 bytes) of 128
+// consecutive rows t of one (b, h), zero-filled past T, in the 128-byte
+// swizzle.  dim_of[0..2]: the map dimension (1..3) holding t, h, b.  False if
+// the driver refuses the layout (the kernel then loads q with threads).
+bool encode_q_tensor_map(CUtensorMap* map, const void* q, int B, int H, int T, int D, const int64_t sq[3], int dtype,
+                         int dim_of[3]) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || (dtype != B2PA_DTYPE_BF16 && dtype != B2PA_DTYPE_F16)) return false;
+  const int64_t ext[3] = {T, H, B};              // logical t, h, b
+  const int64_t str[3] = {sq[2], sq[1], sq[0]};  // their element strides
+  int order[3] = {0, 1, 2};                      // logical dims by increasing stride (t first on ties)
+  for (int i = 1; i < 3; ++i)
+    for (int j = i; j > 0 && str[order[j]] < str[order[j - 1]]; --j) {
+      const int x = order[j];
+      order[j] = order[j - 1];
+      order[j - 1] = x;
+    }
+  cuuint64_t dims[4] = {(cuuint64_t)D, 0, 0, 0};
+  cuuint64_t strides[3];
+  cuuint32_t box[4] = {64, 1, 1, 1};
+  for (int i = 0; i < 3; ++i) {
+    const int l = order[i];
+    if (str[l] <= 0) return false;
+    dims[i + 1] = (cuuint64_t)ext[l];
+    strides[i] = (cuuint64_t)str[l] * 2;
+    box[i + 1] = l == 0 ? 128 : 1;
+    dim_of[l] = i + 1;
+  }
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt = dtype == B2PA_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(map, dt, 4, const_cast<void*>(q), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
 bool encode_pool_tensor_map_uncached(CUtensorMap* map, const void* pool, int64_t rows, int D, int block_size,
                                      int dtype) {
   EncodeTiledFn fn = encode_fn();
