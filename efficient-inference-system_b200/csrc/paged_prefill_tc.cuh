@@ -273,6 +273,53 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
   int* sblk = reinterpret_cast<int*>(smem + C::OFF_BLK);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int split = blockIdx.x % p.nsplit_max;
+  const int t0 = (blockIdx.x / p.nsplit_max) * C::BM;
+  const int h = blockIdx.y;
+  const int b = blockIdx.z;
+  // Q rows -> 128B-swizzled K-major tile, zeros past T, by the softmax
+  // threads (the fp32 variant: hi tile, then lo tile, with the range check);
+  // consecutive threads read consecutive 16-byte pieces of a row.
+  auto load_q_threads = [&]() {
+#pragma unroll
+    for (int it = 0; it < C::BM * D / 8 / C::SOFTMAX_THREADS; ++it) {
+      const int c = tid + it * C::SOFTMAX_THREADS;
+      const int qr = c / (D / 8), qc = c % (D / 8);
+      const int qt = t0 + qr;
+      const int off = (qc >> 3) * (C::BM * 128) + tc::sw128_offset(qr, qc & 7);
+      if constexpr (SPLIT) {
+        float f[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) f[e] = 0.f;
+        if (qt < p.T) {
+          const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.q) + (int64_t)b * p.sq_b +
+                                                              (int64_t)h * p.sq_h + (int64_t)qt * p.sq_t + qc * 8);
+          const float4 x0 = src[0], x1 = src[1];
+          f[0] = x0.x; f[1] = x0.y; f[2] = x0.z; f[3] = x0.w;
+          f[4] = x1.x; f[5] = x1.y; f[6] = x1.z; f[7] = x1.w;
+          bool in_range = true;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) in_range = in_range && fabsf(f[e]) < kSplitRange;
+          if (!in_range) *p.range_flag = p.epoch;
+        }
+        uint4 hi, lo;
+        split_f16x8(f, hi, lo);
+        *reinterpret_cast<uint4*>(sQ + off) = hi;
+        *reinterpret_cast<uint4*>(sQ + C::Q_TILE + off) = lo;
+      } else {
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (qt < p.T)
+          v = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + (int64_t)b * p.sq_b +
+                                              (int64_t)h * p.sq_h + (int64_t)qt * p.sq_t + qc * 8);
+        *reinterpret_cast<uint4*>(sQ + off) = v;
+      }
+    }
+  };
+  // The fp32 variant's q is not written by its pre-pass: the softmax threads
+  // split it while the pre-pass still runs.
+  if constexpr (SPLIT) {
+    if (tid < C::SOFTMAX_THREADS) load_q_threads();
+  }
   // Launched programmatically after the kernel before it (the KV append of
   // the step, or the fp32 variant's pre-pass): wait for its results before
   // reading anything (after the append kernel, only before reading pool
@@ -288,10 +335,6 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
     __syncthreads();
     if (stop) return;
   }
-  const int split = blockIdx.x % p.nsplit_max;
-  const int t0 = (blockIdx.x / p.nsplit_max) * C::BM;
-  const int h = blockIdx.y;
-  const int b = blockIdx.z;
   const int j0 = split * p.kt_per_split;
   const int64_t pg0 = (int64_t)j0 * C::PAGES;
   const int32_t* pt_row = p.page_table + (int64_t)b * p.pt_stride;
@@ -514,44 +557,9 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
     const int g = warp >> 2;     // softmax group
     const int r = tid & 127;     // query row (TMEM lane) of this thread
     const int t = t0 + r;
-    // Q rows -> 128B-swizzled K-major tile, zeros past T; consecutive
-    // threads read consecutive 16-byte pieces of a row (unless the TMA load
-    // of Q, issued at kernel entry, brings it).
-    if (!p.q_tma) {
-#pragma unroll
-    for (int it = 0; it < C::BM * D / 8 / C::SOFTMAX_THREADS; ++it) {
-      const int c = tid + it * C::SOFTMAX_THREADS;
-      const int qr = c / (D / 8), qc = c % (D / 8);
-      const int qt = t0 + qr;
-      const int off = (qc >> 3) * (C::BM * 128) + tc::sw128_offset(qr, qc & 7);
-      if constexpr (SPLIT) {
-        float f[8];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) f[e] = 0.f;
-        if (qt < p.T) {
-          const float4* src = reinterpret_cast<const float4*>(static_cast<const float*>(p.q) + (int64_t)b * p.sq_b +
-                                                              (int64_t)h * p.sq_h + (int64_t)qt * p.sq_t + qc * 8);
-          const float4 x0 = src[0], x1 = src[1];
-          f[0] = x0.x; f[1] = x0.y; f[2] = x0.z; f[3] = x0.w;
-          f[4] = x1.x; f[5] = x1.y; f[6] = x1.z; f[7] = x1.w;
-          bool in_range = true;
-#pragma unroll
-          for (int e = 0; e < 8; ++e) in_range = in_range && fabsf(f[e]) < kSplitRange;
-          if (!in_range) *p.range_flag = p.epoch;
-        }
-        uint4 hi, lo;
-        split_f16x8(f, hi, lo);
-        *reinterpret_cast<uint4*>(sQ + off) = hi;
-        *reinterpret_cast<uint4*>(sQ + C::Q_TILE + off) = lo;
-      } else {
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (qt < p.T)
-          v = *reinterpret_cast<const uint4*>(static_cast<const T*>(p.q) + (int64_t)b * p.sq_b +
-                                              (int64_t)h * p.sq_h + (int64_t)qt * p.sq_t + qc * 8);
-        *reinterpret_cast<uint4*>(sQ + off) = v;
-      }
-    }
-    }
+    // Q: by TMA (issued at kernel entry), by these threads here (16-bit q
+    // the tensor map does not take), or already split at kernel entry (fp32).
+    if (!SPLIT && !p.q_tma) load_q_threads();
     tc::fence_proxy_async_smem();
     tc::fence_before_sync();
     named_bar_sync(1, C::THREADS);
