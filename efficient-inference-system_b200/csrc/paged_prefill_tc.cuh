@@ -930,23 +930,31 @@ __global__ void __launch_bounds__(128) prefill_split_pages_kernel(PfSplitArgs a)
     const int r = idx / (D / 8), c8 = idx - (idx / (D / 8)) * (D / 8);
     const int64_t pos = (int64_t)i * BS + r;
     const bool fresh = pos >= app_lo && pos < app_hi;
+    // Both rows (K and V) are loaded before anything is stored, so the four
+    // 16-byte loads are in flight together (the stores below could alias
+    // them as far as the compiler knows).
+    float4 x[2][2];
 #pragma unroll
     for (int kv = 0; kv < 2; ++kv) {
-      float* pool_row = (kv ? a.v_pool : a.k_pool) + src + (int64_t)r * D + c8 * 8;
-      float4 x0, x1;
+      const float4* s4;
       if (fresh) {
         const int64_t t = pos - app_lo;
         const int64_t* sn = kv ? a.svn : a.skn;
-        const float4* n4 = reinterpret_cast<const float4*>((kv ? a.v_new : a.k_new) + (int64_t)b * sn[0] +
-                                                           (int64_t)h * sn[1] + t * sn[2] + c8 * 8);
-        x0 = n4[0];
-        x1 = n4[1];
+        s4 = reinterpret_cast<const float4*>((kv ? a.v_new : a.k_new) + (int64_t)b * sn[0] + (int64_t)h * sn[1] +
+                                             t * sn[2] + c8 * 8);
+      } else {
+        s4 = reinterpret_cast<const float4*>((kv ? a.v_pool : a.k_pool) + src + (int64_t)r * D + c8 * 8);
+      }
+      x[kv][0] = s4[0];
+      x[kv][1] = s4[1];
+    }
+#pragma unroll
+    for (int kv = 0; kv < 2; ++kv) {
+      const float4 x0 = x[kv][0], x1 = x[kv][1];
+      if (fresh) {
+        float* pool_row = (kv ? a.v_pool : a.k_pool) + src + (int64_t)r * D + c8 * 8;
         reinterpret_cast<float4*>(pool_row)[0] = x0;
         reinterpret_cast<float4*>(pool_row)[1] = x1;
-      } else {
-        const float4* s4 = reinterpret_cast<const float4*>(pool_row);
-        x0 = s4[0];
-        x1 = s4[1];
       }
       const float f[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
