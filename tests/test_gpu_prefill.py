@@ -189,3 +189,28 @@ def test_prefill_f32_outside_split_range_is_recomputed(cuda_device, where):
     _check(out, ref, torch.float32)
     assert np.isfinite(out.cpu().numpy()).all()
     assert b2pa.read_status(cuda_device) == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_prefill_q_layout_without_tensor_map(cuda_device, dtype):
+    """16-bit q is loaded with a TMA tensor map when its layout allows one;
+    a q expanded along the batch (stride 0) is refused by the map encoder,
+    and the kernel then loads Q with its softmax threads -- same results."""
+    rng = np.random.default_rng(41)
+    gen = torch.Generator().manual_seed(41)
+    B, H, D, bs, T = 3, 2, 64, 16, 150
+    prefixes, curs = [40, 0, 300], [150, 90, 150]
+    lens = [p + c for p, c in zip(prefixes, curs)]
+    NB = sum(-(-L // bs) for L in lens) + 4
+    kp = torch.randn(NB, H, bs, D, generator=gen).to(dtype).to(cuda_device)
+    vp = torch.randn(NB, H, bs, D, generator=gen).to(dtype).to(cuda_device)
+    tables = random_tables(rng, lens, NB, bs)
+    cache = build_cache(b2pa, kp, vp, tables, lens, bs)
+    q1 = torch.randn(1, H, T, D, generator=gen).to(dtype).to(cuda_device)
+    q = q1.expand(B, H, T, D)
+    assert q.stride(0) == 0
+    out = b2pa.paged_attention("b200_paged", q, cache, torch.tensor(curs))
+    ref = orc.paged_attention_c(q.float().cpu().numpy(), kp.float().cpu().numpy(), vp.float().cpu().numpy(), tables,
+                                lens, curs)
+    _check(out, ref, dtype)
+    assert b2pa.read_status(cuda_device) == 0
