@@ -117,12 +117,19 @@ int launch_zero_blocks(const ZeroArgs& a, cudaStream_t stream);
 int launch_patch_table(int32_t* table, int64_t n_cells, const int32_t* pairs, int n_pairs, int32_t* status,
                        cudaStream_t stream);
 
+// Contiguous decode split: a CTA takes at least kDecodeMinUnits pages, and
+// the launch is capped at kDecodeMaxCtasPerSm CTAs per SM (two partial slots
+// each in the workspace).
+constexpr int kDecodeMinUnits = 4;
+constexpr int kDecodeMaxCtasPerSm = 8;
+
 // Decode planning shared by the workspace query and the launcher.
 struct DecodePlan {
   int G;                // heads per CTA (consumer warps)
   int HG;               // head groups = H / G
-  int pages_per_split;  // P
-  int64_t max_items;    // upper bound on work items
+  int pages_per_split;  // P (item split)
+  int contig;           // 1: contiguous split (per-CTA ranges of pages)
+  int64_t max_items;    // upper bound on work items (contiguous split: partial slots)
   size_t off_item_off, off_part_ml, off_part_acc, bytes;
 };
 DecodePlan make_decode_plan(int B, int H, int D, int max_pages, int block_size, int dtype);

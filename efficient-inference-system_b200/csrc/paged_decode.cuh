@@ -86,6 +86,12 @@ struct DecodeParams {
   int64_t so_b, so_h;
   int B, H, G, HG;
   int pages_per_split;
+  // 1: contiguous split -- CTA c streams units [c*W/Gu, (c+1)*W/Gu) of the
+  // flattened (sequence, head group, page) sequence; 0: items of
+  // pages_per_split pages, strided over the grid.
+  int contig;
+  int min_units;    // contiguous split: a CTA takes at least this many units
+  int grid_launch;  // CTAs launched (the combine kernel recomputes the split from it)
   int stages;
   int stage_bytes;
   int meta_off;  // offset of StageMeta inside a stage
@@ -118,6 +124,7 @@ struct StageMeta {
 };
 constexpr int kFirst = 1;
 constexpr int kLast = 2;
+constexpr int kEnd = 4;  // the CTA's last item
 
 // Visible key count of sequence b, clamped to the page table width.
 __device__ __forceinline__ int decode_visible(const DecodeParams& p, int b, int bs) {
@@ -131,7 +138,45 @@ __device__ __forceinline__ int decode_visible(const DecodeParams& p, int b, int 
   return (int)e;
 }
 
-// One CTA: item_off[b] = HG * sum_{b' < b} nsplit(b'), item_off[B] = total.
+// Offsets counted per sequence b: HG * number of items (splits of
+// pages_per_split pages, at least one), or for the contiguous split HG *
+// units (visible pages, at least one, so that a stream with no visible key
+// still writes its zeros).
+template <int BS>
+__device__ __forceinline__ int decode_items_of(const DecodeParams& p, int b) {
+  const int vis = decode_visible(p, b, BS);
+  const int np = (vis + BS - 1) / BS;
+  const int n = p.contig ? np : (np + p.pages_per_split - 1) / p.pages_per_split;
+  return (n < 1 ? 1 : n) * p.HG;
+}
+
+// The contiguous split (32-bit arithmetic: the host keeps B * HG *
+// max_pages below 2^31).  Gu = CTAs in use, about one per min_units units,
+// at least one, at most the launch.  With q = W / Gu and r = W % Gu, CTA c
+// takes q units, plus one for the first r CTAs; its first unit is
+// c*q + min(c, r) (Gu <= W, so q >= 1).  decode_cta_of inverts it;
+// decode_slot is the partial slot of the piece of a stream starting at unit
+// `sstart` that CTA c holds: 2c when the stream reaches back to the CTA's
+// first unit (its first piece), else 2c + 1 (only these two can be cut).
+__device__ __forceinline__ int decode_ctas_used(const DecodeParams& p, int W) {
+  int g = W / p.min_units + (W % p.min_units != 0);
+  if (g > p.grid_launch) g = p.grid_launch;
+  return g < 1 ? 1 : g;
+}
+__device__ __forceinline__ int decode_start(int c, int W, int Gu) {
+  const int q = W / Gu, r = W - (W / Gu) * Gu;
+  return c * q + (c < r ? c : r);
+}
+__device__ __forceinline__ int decode_cta_of(int w, int W, int Gu) {
+  const int q = W / Gu, r = W - (W / Gu) * Gu;
+  const int big = r * (q + 1);
+  return w < big ? w / (q + 1) : r + (w - big) / q;
+}
+__device__ __forceinline__ int decode_slot(int c, int sstart, int W, int Gu) {
+  return 2 * c + (sstart > decode_start(c, W, Gu) ? 1 : 0);
+}
+
+// One CTA: item_off[b] = prefix of decode_items_of, item_off[B] = total.
 template <int BS>
 __global__ void __launch_bounds__(1024) decode_plan_kernel(DecodeParams p) {
   __shared__ int warp_sums[32];
@@ -145,10 +190,7 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(DecodeParams p) {
     if (b < p.B) {
       const int64_t L = p.seq_lens[b];
       if (L > (int64_t)p.max_pages * BS) set_status(p.status, B2PA_ERR_BAD_BLOCK_ID);
-      const int vis = decode_visible(p, b, BS);
-      const int np = (vis + BS - 1) / BS;
-      int ns = (np + p.pages_per_split - 1) / p.pages_per_split;
-      n = (ns < 1 ? 1 : ns) * p.HG;
+      n = decode_items_of<BS>(p, b);
     }
     int x = n;
 #pragma unroll
@@ -175,15 +217,6 @@ __global__ void __launch_bounds__(1024) decode_plan_kernel(DecodeParams p) {
     __syncthreads();
   }
   if (tid == 0) p.item_off[p.B] = carry;
-}
-
-// Items of sequence b: HG * number of splits (at least one split).
-template <int BS>
-__device__ __forceinline__ int decode_items_of(const DecodeParams& p, int b) {
-  const int vis = decode_visible(p, b, BS);
-  const int np = (vis + BS - 1) / BS;
-  const int ns = (np + p.pages_per_split - 1) / p.pages_per_split;
-  return (ns < 1 ? 1 : ns) * p.HG;
 }
 
 // The plan of decode_plan_kernel computed by one CTA of the decode kernel
@@ -362,12 +395,24 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
     uint32_t issued = 0, issued_par = 0;  // per-stage bookkeeping for drain
     int cur_b = 0;
     bool ok = true;
-    for (int w = blockIdx.x; w < total && ok; w += gridDim.x) {
-      // Locate the sequence of item w (items are visited in increasing order).
+    // Item split: item w, then w + gridDim.x, ...  Contiguous split: the
+    // units [u, uend) of this CTA, one piece (a run of units of one stream)
+    // at a time.
+    int w = blockIdx.x, u = 0, uend = 0, Gu = 1;
+    if (p.contig) {
+      Gu = decode_ctas_used(p, total);
+      if ((int)blockIdx.x < Gu) {
+        u = decode_start(blockIdx.x, total, Gu);
+        uend = decode_start(blockIdx.x + 1, total, Gu);
+      }
+    }
+    while (ok && (p.contig ? u < uend : w < total)) {
+      const int key = p.contig ? u : w;
+      // Locate the sequence of unit/item `key` (visited in increasing order).
       while (true) {
         const int idx = cur_b + 1 + lane;
         const int v = idx <= p.B ? off[idx] : INT_MAX;
-        const unsigned m = __ballot_sync(kFullMask, v > w);
+        const unsigned m = __ballot_sync(kFullMask, v > key);
         if (m) {
           cur_b += __ffs(m) - 1;
           break;
@@ -376,21 +421,44 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
       }
       const int b = cur_b;
       const int off0 = off[b];
-      const int nsplit = (off[b + 1] - off0) / p.HG;
-      const int r = w - off0;
-      const int hg = r / nsplit;
-      const int s = r - hg * nsplit;
+      const int per = (off[b + 1] - off0) / p.HG;  // items or units per stream
+      const int r = key - off0;
+      const int hg = r / per;
+      const int s = r - hg * per;
       const int vis = decode_visible(p, b, BS);
       const int npages = (vis + BS - 1) / BS;
-      const int p0 = s * p.pages_per_split;
-      int p1 = p0 + p.pages_per_split;
+      int p0, span, count, item, nsplit, flags_end = 0;
+      bool stream_tail;  // the piece holds the stream's last page
+      if (p.contig) {
+        // Units s .. se-1 of the stream are pages s .. se-1 (one unit and
+        // no page when nothing is visible).
+        const int left = uend - u;
+        const int se = per - s < left ? per : s + left;
+        p0 = s;
+        span = se - s;
+        count = span;
+        const bool whole = s == 0 && se == per;
+        item = whole ? 0 : decode_slot(blockIdx.x, u - s, total, Gu);
+        nsplit = whole ? 1 : 2;
+        stream_tail = se == per;
+        if (u + count == uend) flags_end = kEnd;
+        u += count;
+      } else {
+        p0 = s * p.pages_per_split;
+        span = p.pages_per_split;
+        item = w;
+        nsplit = per;
+        stream_tail = s == per - 1;
+        w += gridDim.x;
+      }
+      int p1 = p0 + span;
       p1 = p1 < npages ? p1 : npages;
       const int npg = p1 > p0 ? p1 - p0 : 0;
-      const int count = npg > 0 ? npg : 1;
+      if (!p.contig) count = npg > 0 ? npg : 1;
       const int h0 = hg * G;
       const char* kbase = static_cast<const char*>(p.k_pool);
       const char* vbase = static_cast<const char*>(p.v_pool);
-      if (p.app_len != nullptr && s == nsplit - 1) decode_append_rows<T, D, BS>(p, b, h0, G, lane);
+      if (p.app_len != nullptr && stream_tail) decode_append_rows<T, D, BS>(p, b, h0, G, lane);
 
       for (int i0 = 0; i0 < count && ok; i0 += 32) {
         int blk = -1;
@@ -442,10 +510,10 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
             }
             meta->b = b;
             meta->h0 = h0;
-            meta->item = w;
+            meta->item = item;
             meta->nsplit = nsplit;
             meta->nvalid = nv;
-            meta->flags = (pi == 0 ? kFirst : 0) | (pi == count - 1 ? kLast : 0);
+            meta->flags = (pi == 0 ? kFirst : 0) | (pi == count - 1 ? kLast | flags_end : 0);
           }
           __threadfence_block();
           __syncwarp();
@@ -476,7 +544,12 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
   const int r_own = rg + Tile::RP * (c >> Tile::SH);
   int stage = 0;
   uint32_t phase = 0;
-  for (int w = blockIdx.x; w < total; w += gridDim.x) {
+  // Item split: the producer's items w = blockIdx.x, + gridDim.x, ...
+  // Contiguous split: pieces until the one flagged kEnd (none for a CTA past
+  // the ones in use).
+  int w = blockIdx.x;
+  bool more = p.contig ? (int)blockIdx.x < decode_ctas_used(p, total) : w < total;
+  while (more) {
     float q[Tile::CPL][Tile::CH];
     float acc[Tile::CPL][Tile::CH];
     float m = -INFINITY, l_part = 0.f;
@@ -588,16 +661,26 @@ __global__ void __launch_bounds__(160) paged_decode_kernel(DecodeParams p) {
             p.part_ml[2 * slot + 1] = l;
           }
         }
+        if (p.contig) {
+          more = (meta.flags & kEnd) == 0;
+        } else {
+          w += gridDim.x;
+          more = w < total;
+        }
         break;
       }
     }
   }
 }
 
-// One warp per (sequence, head) whose sequence was split: log-sum-exp merge.
+// One warp per (sequence, head) whose stream was split: log-sum-exp merge.
 // The split statistics are read one split per lane and reduced across the
 // warp, and the partial accumulators are read with independent loads (the
 // weights come by shuffle), so the merge is not a chain of dependent loads.
+// Item split: the stream's splits are items base .. base+nsplit-1.
+// Contiguous split: its pieces are held by CTAs c0 .. c1 (the CTAs of its
+// first and last unit), piece j in slot decode_slot(c0 + j, ...); a stream
+// inside one CTA was written directly.
 template <typename T, int D>
 __global__ void __launch_bounds__(256) decode_combine_kernel(DecodeParams p) {
   pdl_wait();
@@ -607,13 +690,23 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(DecodeParams p) {
   const int b = (int)(gw / p.H);
   const int h = (int)(gw - (int64_t)b * p.H);
   const int off0 = p.item_off[b];
-  const int nsplit = (p.item_off[b + 1] - off0) / p.HG;
-  if (nsplit <= 1) return;
+  const int per = (p.item_off[b + 1] - off0) / p.HG;
   const int hg = h / p.G;
   const int hi = h - hg * p.G;
-  const int64_t base = (int64_t)off0 + (int64_t)hg * nsplit;
+  const int64_t base = (int64_t)off0 + (int64_t)hg * per;  // the stream's first item / unit
+  int nsplit = per, c0 = 0, W = 0, Gu = 1;
+  if (p.contig) {
+    W = p.item_off[p.B];
+    Gu = decode_ctas_used(p, W);
+    c0 = decode_cta_of((int)base, W, Gu);
+    nsplit = decode_cta_of((int)base + per - 1, W, Gu) - c0 + 1;
+  }
+  if (nsplit <= 1) return;
+  auto slot_of = [&](int s) -> int64_t {
+    return p.contig ? (int64_t)decode_slot(c0 + s, (int)base, W, Gu) : base + s;
+  };
   float M = -INFINITY;
-  for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, p.part_ml[2 * ((base + s) * p.G + hi)]);
+  for (int s = lane; s < nsplit; s += 32) M = fmaxf(M, p.part_ml[2 * (slot_of(s) * p.G + hi)]);
   M = warp_max(M);
   constexpr int PER = D >= 32 ? D / 32 : 1;
   float o[PER];
@@ -624,7 +717,7 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(DecodeParams p) {
     const int s = s0 + lane;
     float wl = 0.f;
     if (s < nsplit) {
-      const int64_t slot = (base + s) * p.G + hi;
+      const int64_t slot = slot_of(s) * p.G + hi;
       const float ms = p.part_ml[2 * slot];
       wl = (M == -INFINITY) ? 0.f : exp2f(ms - M);
       L = fmaf(p.part_ml[2 * slot + 1], wl, L);
@@ -633,7 +726,7 @@ __global__ void __launch_bounds__(256) decode_combine_kernel(DecodeParams p) {
 #pragma unroll 4
     for (int j = 0; j < cnt; ++j) {
       const float wgt = __shfl_sync(kFullMask, wl, j);
-      const float* pa = p.part_acc + ((base + s0 + j) * p.G + hi) * D;
+      const float* pa = p.part_acc + (slot_of(s0 + j) * p.G + hi) * D;
 #pragma unroll
       for (int i = 0; i < PER; ++i) {
         const int d = lane + 32 * i;
@@ -676,6 +769,8 @@ int launch_decode_impl(const AttnArgs& a, const DecodePlan& plan, cudaStream_t s
   p.G = plan.G;
   p.HG = plan.HG;
   p.pages_per_split = plan.pages_per_split;
+  p.contig = plan.contig;
+  p.min_units = kDecodeMinUnits;
   p.qscale = a.scale * kLog2e;
   char* ws = static_cast<char*>(a.workspace);
   p.item_off = reinterpret_cast<int32_t*>(ws + plan.off_item_off);
@@ -719,13 +814,17 @@ int launch_decode_impl(const AttnArgs& a, const DecodePlan& plan, cudaStream_t s
   const int per_sm = decode_occupancy_cached(reinterpret_cast<const void*>(kern), threads, smem);
   if (per_sm <= 0) return set_error(B2PA_ERR_UNSUPPORTED, "paged_decode: kernel does not fit on an SM");
   int64_t grid = (int64_t)device_sm_count() * per_sm;
-  if (grid > plan.max_items) grid = plan.max_items;
+  // Contiguous split: two partial slots per CTA; item split: no more CTAs
+  // than items.
+  const int64_t cap = plan.contig ? plan.max_items / 2 : plan.max_items;
+  if (grid > cap) grid = cap;
   if (grid < 1) grid = 1;
+  p.grid_launch = (int)grid;
 
   if (!p.plan_in_smem) decode_plan_kernel<BS><<<1, 1024, 0, stream>>>(p);
   e = launch_pdl(kern, dim3((unsigned)grid), dim3(threads), smem, stream, p);
   if (e != cudaSuccess) return set_error(B2PA_ERR_CUDA, "paged_decode launch: %s", cudaGetErrorString(e));
-  if (plan.max_items > (int64_t)a.B * plan.HG) {  // some sequence may be split
+  if (plan.contig || plan.max_items > (int64_t)a.B * plan.HG) {  // some stream may be split
     const int64_t warps = (int64_t)a.B * a.H;
     const unsigned cgrid = (unsigned)((warps + 7) / 8);
     e = launch_pdl(decode_combine_kernel<T, D>, dim3(cgrid), dim3(256), 0, stream, p);

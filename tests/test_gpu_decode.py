@@ -84,6 +84,36 @@ def test_decode_many_sequences_plan(cuda_device):
     _check(out, ref, torch.float32)
 
 
+def _many_stream_lengths(rng, B):
+    """Mostly short contexts (zeros, block edges) plus three long ones, so
+    that with B * H / 4 >= 2368 head-group streams the contiguous split cuts
+    streams between CTAs, some across many CTAs."""
+    lens = rng.integers(0, 200, size=B)
+    lens[:8] = [0, 1, 15, 16, 17, 32, 0, 33]
+    lens[100], lens[700], lens[B - 1] = 9000, 16000, 12345
+    return lens.tolist()
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 16), (torch.float32, 32)])
+def test_decode_contiguous_split(cuda_device, dtype, D):
+    """2400 head-group streams: each CTA streams an equal range of pages and
+    streams cut between CTAs are merged by the combine kernel; cur_len 0 / 2 /
+    past the length included.  Two calls give the same bytes."""
+    rng = np.random.default_rng(31)
+    B, H = 1200, 8
+    lens = _many_stream_lengths(rng, B)
+    cur = [1] * B
+    cur[3], cur[9], cur[700], cur[11] = 0, 2, 3, 500
+    out, ref = _random_decode(cuda_device, B=B, H=H, D=D, bs=16, dtype=dtype, lmin=0, lmax=0, seed=31, cur=cur,
+                              lens=lens)
+    _check(out, ref, dtype)
+    assert out[6].abs().sum().item() == 0 and out[11].abs().sum().item() == 0
+    again, _ = _random_decode(cuda_device, B=B, H=H, D=D, bs=16, dtype=dtype, lmin=0, lmax=0, seed=31, cur=cur,
+                              lens=lens)
+    assert torch.equal(out, again)
+    assert b2pa.read_status(cuda_device) == 0
+
+
 def test_decode_long_contexts_split(cuda_device):
     # few sequences, long contexts: many pages per sequence -> split-K + combine
     out, ref = _random_decode(cuda_device, B=3, H=8, D=128, bs=16, dtype=torch.bfloat16, lmin=4000, lmax=9000,

@@ -171,6 +171,19 @@ def test_fused_long_sequences_bf16(cuda_device):
     _compare(pr, cuda_device)
 
 
+def test_fused_contiguous_split(cuda_device):
+    # 1200 sequences x 2 head groups: the contiguous split, with the append
+    # done by the CTA whose piece holds each stream's last page
+    rng = np.random.default_rng(12)
+    lens_old = rng.integers(0, 150, size=1200)
+    lens_old[:4] = [0, 15, 16, 31]
+    lens_old[500], lens_old[1199] = 7000, 4097
+    cur = [1] * 1200
+    cur[4], cur[5] = 2, 0
+    pr = _problem(cuda_device, H=8, D=16, bs=16, dtype=torch.bfloat16, lens_old=lens_old.tolist(), cur=cur, seed=12)
+    _compare(pr, cuda_device)
+
+
 def test_fused_bad_position_and_block_reported(cuda_device):
     """A start position other than seq_len - 1 and a block id past the pool
     end are skipped and reported; the pools keep their bytes."""

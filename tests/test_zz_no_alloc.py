@@ -97,8 +97,9 @@ def test_noalloc_decode_matches_workspace_decode_twice(cuda_device):
 
 def test_noalloc_rejects_problems_larger_than_the_array(cuda_device):
     lib = _lib.load()
-    # 512 sequences x 32 heads x 8192 tokens needs far more than 32 MiB of partials
-    B, H, D, bs, max_pages = 512, 32, 128, 16, 513
+    # 64 sequences x 32 heads x 65536 tokens (item split: 512 streams x 64
+    # splits) needs far more than 32 MiB of partials
+    B, H, D, bs, max_pages = 64, 32, 128, 16, 4096
     assert lib.b2pa_paged_decode_workspace_size(B, H, D, max_pages, bs, _lib.DTYPE_BF16) > SCRATCH_BYTES
     q = torch.zeros(B, H, 1, D, dtype=torch.bfloat16, device=cuda_device)
     pool = torch.zeros(4, H, bs, D, dtype=torch.bfloat16, device=cuda_device)
