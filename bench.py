@@ -65,6 +65,9 @@ def parse_args(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true",
                     help="skip the config[1] / config[2] kernel timings in the main line (N=1)")
+    ap.add_argument("--len-range", type=int, nargs=2, default=None, metavar=("LO", "HI"),
+                    help="context lengths U[LO,HI] instead of config[4]'s U[1024,8192] (small profiling cases; "
+                         "the line then names the range)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="target CPU work of the baseline sample")
     ap.add_argument("--decode-append", choices=["separate", "fused"], default="fused",
                     help="separate: b2pa_kv_append then b2pa_paged_decode per step; fused: one "
@@ -76,9 +79,9 @@ def parse_args(argv=None):
 
 
 # --------------------------------------------------------------- workload
-def all_lengths(total: int) -> np.ndarray:
+def all_lengths(total: int, lo: int = LMIN, hi: int = LMAX) -> np.ndarray:
     rng = np.random.default_rng(SEED)
-    return rng.integers(LMIN, LMAX + 1, size=total)
+    return rng.integers(lo, hi + 1, size=total)
 
 
 def balanced_partition(lens: np.ndarray, world: int) -> list[np.ndarray]:
@@ -106,7 +109,8 @@ def my_sequences(args, rank: int, world: int, scaling: str | None = None) -> np.
     of ``seqs * world`` sequences (``seqs`` per GPU); strong: the fixed draw
     of ``seqs``; either way spread over the ranks by ``balanced_partition``."""
     scaling = scaling or args.scaling
-    lens = all_lengths(args.seqs * world if scaling == "weak" else args.seqs)
+    lo, hi = getattr(args, "len_range", None) or (LMIN, LMAX)
+    lens = all_lengths(args.seqs * world if scaling == "weak" else args.seqs, lo, hi)
     return lens[balanced_partition(lens, world)[rank]]
 
 
@@ -718,6 +722,7 @@ def main(argv=None) -> int:
             "pool_gb_per_gpu": pool_gb,
             "parallelism": f"sequence-partitioned dp{world}, one pool per rank, no hot-path collective",
             "l2": "inputs larger than L2 (K/V pool of tens of GB per GPU); no flush needed",
+            **({"len_range": "U[%d,%d], not config[4]'s" % tuple(args.len_range)} if args.len_range else {}),
         },
         "hbm_gb_per_s_decode": achieved_gbs,
         "roofline": {
@@ -736,7 +741,10 @@ def main(argv=None) -> int:
             "decode_ms_per_launch": decode_avg_ms,
             # DRAM bytes per launch: the ncu capture of this kernel on the
             # 16-sequence case (1.4386 GB read + 6.6 MB written for 1.4373 GB
-            # algorithmic) scaled to this launch by its algorithmic bytes
+            # algorithmic) scaled to this launch by its algorithmic bytes; its
+            # long contexts have config[4]'s share of partial last pages (a
+            # 300-sequence capture of the contiguous split read the
+            # algorithmic bytes plus its page tails within 0.03 %)
             "traffic": bytes_per_launch * DECODE_TRAFFIC_PER_ALGORITHMIC_BYTE,
             "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum of the 16-sequence capture, "
                               "scaled by algorithmic bytes",
