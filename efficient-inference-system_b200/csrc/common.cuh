@@ -12,6 +12,8 @@
 #include <cuda_fp16.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 #include "b2pa.h"
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
@@ -92,10 +94,22 @@ struct Vec {
     }
   }
 
+  // 16-bit types convert two values per instruction (round to nearest,
+  // the same bits as two single conversions).
   __device__ __forceinline__ void from_float(const float* f) {
-    T* p = reinterpret_cast<T*>(&w);
+    if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+      __nv_bfloat162* p = reinterpret_cast<__nv_bfloat162*>(&w);
 #pragma unroll
-    for (int i = 0; i < N; ++i) p[i] = from_f32<T>(f[i]);
+      for (int i = 0; i < N / 2; ++i) p[i] = __floats2bfloat162_rn(f[2 * i], f[2 * i + 1]);
+    } else if constexpr (std::is_same<T, __half>::value) {
+      __half2* p = reinterpret_cast<__half2*>(&w);
+#pragma unroll
+      for (int i = 0; i < N / 2; ++i) p[i] = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
+    } else {
+      T* p = reinterpret_cast<T*>(&w);
+#pragma unroll
+      for (int i = 0; i < N; ++i) p[i] = from_f32<T>(f[i]);
+    }
   }
 };
 
@@ -192,6 +206,14 @@ __device__ __forceinline__ float fast_exp2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Maximum of three fp32 values in one instruction (sm_100 `max.f32` with
+// three sources); exact, like two fmaxf.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 // Packed two-lane fp32 arithmetic of sm_100 (one instruction for two

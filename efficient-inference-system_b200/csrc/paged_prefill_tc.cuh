@@ -233,8 +233,9 @@ __device__ __forceinline__ void split_f16x8(const float (&f)[8], uint4& hi, uint
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     const __half2 hh = __floats2half2_rn(f[2 * i], f[2 * i + 1]);
-    const float2 hf = __half22float2(hh);
-    const __half2 ll = __floats2half2_rn(f[2 * i] - hf.x, f[2 * i + 1] - hf.y);
+    // x - hi as one packed fma with -1 (exact: the same bits as x - hi)
+    const float2 r = fma2(__half22float2(hh), make_float2(-1.f, -1.f), make_float2(f[2 * i], f[2 * i + 1]));
+    const __half2 ll = __floats2half2_rn(r.x, r.y);
     h[i] = *reinterpret_cast<const uint32_t*>(&hh);
     l[i] = *reinterpret_cast<const uint32_t*>(&ll);
   }
@@ -641,14 +642,14 @@ __global__ void __launch_bounds__(PfTcCfg<D, BS, kPfSplit<T>>::THREADS, 1)
           s[e] = vis ? s[e] : -INFINITY;
         }
       }
-      // Row max as a tree (short dependency chains).
+      // Row max as a tree of three-input maxima (short dependency chains,
+      // 36 instructions for 64 values).
       float mx[8];
 #pragma unroll
-      for (int e = 0; e < 8; ++e) mx[e] = fmaxf(fmaxf(s[e], s[e + 8]), fmaxf(s[e + 16], s[e + 24]));
-#pragma unroll
-      for (int e = 0; e < 8; ++e) mx[e] = fmaxf(mx[e], fmaxf(fmaxf(s[e + 32], s[e + 40]), fmaxf(s[e + 48], s[e + 56])));
-      const float mt =
-          sc * fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+      for (int e = 0; e < 8; ++e)
+        mx[e] = fmax3(fmax3(s[e], s[e + 8], s[e + 16]), fmax3(s[e + 24], s[e + 32], s[e + 40]),
+                      fmaxf(s[e + 48], s[e + 56]));
+      const float mt = sc * fmax3(fmax3(mx[0], mx[1], mx[2]), fmax3(mx[3], mx[4], mx[5]), fmaxf(mx[6], mx[7]));
       // A row moves its reference max when the tile's max exceeds it by more
       // than kRescale.  Rows that already hold O at the old scale need O and
       // l multiplied by 2^(m_old - m_new); a row with no visible key so far
