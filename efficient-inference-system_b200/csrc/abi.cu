@@ -135,14 +135,21 @@ DecodePlan make_decode_plan(int B, int H, int D, int max_pages, int block_size, 
   pl.max_items = (int64_t)B * pl.HG * (splits > 0 ? splits : 1);
   // Contiguous split (each CTA streams an equal range of the flattened
   // (sequence, head group, page) units; a stream cut between CTAs leaves one
-  // partial per piece) when there are at least two streams per CTA slot.
-  // It balances the SMs exactly and took config[4] (4096 streams) from 87.2k
-  // to 89.9k tok/s, but with few streams the extra pieces cost more than the
-  // balance saves (config[1], 128 streams: 33.2 -> 34.8 us; config[0]: 170 ->
-  // 179-202 us), so those keep the item split.
+  // partial per piece) when there are at least as many streams as a typical
+  // grid has CTAs (148 SMs x 3).  Then the item split has more than one item
+  // per CTA and quantises into waves, while the ranges balance the SMs
+  // exactly; with fewer streams the item split measured faster (the extra
+  // pieces of the ranges cost more than they save).  Measured per decode
+  // call (bf16, H=32, D=128 unless noted; short: L ~ U[128,1024], long:
+  // U[1024,8192]; item -> contiguous split): 128 streams
+  // (config[1], fp32, H=8, D=64) 33.6 -> 36.6 us; 128 long streams 224.7 ->
+  // 228.5 us; 256 short streams 69.7 -> 75.5 us; 512 short streams 165.1 ->
+  // 124.8 us; 512 / 1,024 / 2,048 / 4,096 long streams (config[4], 64 to
+  // 512 sequences) 4.8 / 2.7 / 2.2 / 2.9 % faster.
   const int64_t max_ctas = (int64_t)device_sm_count() * kDecodeMaxCtasPerSm;
   const int64_t units = (int64_t)B * pl.HG * (max_pages > 0 ? max_pages : 1);
-  pl.contig = (int64_t)B * pl.HG >= 2 * max_ctas && units <= INT32_MAX ? 1 : 0;
+  pl.contig =
+      (int64_t)B * pl.HG >= (int64_t)kDecodeContigStreamsPerSm * device_sm_count() && units <= INT32_MAX ? 1 : 0;
   if (pl.contig) pl.max_items = 2 * max_ctas;
   size_t off = 0;
   pl.off_item_off = off;

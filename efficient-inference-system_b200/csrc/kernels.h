@@ -120,8 +120,10 @@ int launch_patch_table(int32_t* table, int64_t n_cells, const int32_t* pairs, in
 // Contiguous decode split: a CTA takes at least kDecodeMinUnits pages, and
 // the launch is capped at kDecodeMaxCtasPerSm CTAs per SM (two partial slots
 // each in the workspace).
+// The plan takes it from kDecodeContigStreamsPerSm head-group streams per SM.
 constexpr int kDecodeMinUnits = 4;
 constexpr int kDecodeMaxCtasPerSm = 8;
+constexpr int kDecodeContigStreamsPerSm = 3;
 
 // Decode planning shared by the workspace query and the launcher.
 struct DecodePlan {

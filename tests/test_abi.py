@@ -151,9 +151,12 @@ def test_workspace_size_is_monotone(lib):
     assert c > 0 and c % 256 == 0
     assert f(0, 8, 64, 65, 16, 0) == 0
     # 4096 head-group streams (config[4]): the contiguous split keeps two
-    # partial slots per CTA slot, whatever the context length
+    # partial slots per CTA slot, whatever the context length; so do 512
+    # streams, while 256 take the item split (partials grow with the length)
     assert f(512, 32, 128, 1026, 16, 1) == c
     assert c < 8 << 20
+    assert f(64, 32, 128, 4096, 16, 1) < 8 << 20
+    assert f(32, 32, 128, 4096, 16, 1) > 32 << 20
     # fp32, head_dim 64 (tensor cores on fp16 hi/lo splits): the split copies
     # of K and V (B * max_pages slots x H pages x block x 2D halves) + the slot table
     n = lib.b2pa_paged_prefill_workspace_size(8, 8, 256, 64, 32, 16, 0)

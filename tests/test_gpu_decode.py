@@ -86,7 +86,7 @@ def test_decode_many_sequences_plan(cuda_device):
 
 def _many_stream_lengths(rng, B):
     """Mostly short contexts (zeros, block edges) plus three long ones, so
-    that with B * H / 4 >= 2368 head-group streams the contiguous split cuts
+    that with B * H / 4 >= 444 head-group streams the contiguous split cuts
     streams between CTAs, some across many CTAs."""
     lens = rng.integers(0, 200, size=B)
     lens[:8] = [0, 1, 15, 16, 17, 32, 0, 33]

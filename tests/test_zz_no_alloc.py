@@ -97,9 +97,9 @@ def test_noalloc_decode_matches_workspace_decode_twice(cuda_device):
 
 def test_noalloc_rejects_problems_larger_than_the_array(cuda_device):
     lib = _lib.load()
-    # 64 sequences x 32 heads x 65536 tokens (item split: 512 streams x 64
+    # 32 sequences x 32 heads x 131072 tokens (item split: 256 streams x 128
     # splits) needs far more than 32 MiB of partials
-    B, H, D, bs, max_pages = 64, 32, 128, 16, 4096
+    B, H, D, bs, max_pages = 32, 32, 128, 16, 8192
     assert lib.b2pa_paged_decode_workspace_size(B, H, D, max_pages, bs, _lib.DTYPE_BF16) > SCRATCH_BYTES
     q = torch.zeros(B, H, 1, D, dtype=torch.bfloat16, device=cuda_device)
     pool = torch.zeros(4, H, bs, D, dtype=torch.bfloat16, device=cuda_device)
