@@ -114,6 +114,19 @@ def test_decode_contiguous_split(cuda_device, dtype, D):
     assert b2pa.read_status(cuda_device) == 0
 
 
+def test_decode_contiguous_split_plan_kernel(cuda_device):
+    """9,000 sequences: the unit offsets of the contiguous split come from the
+    one-CTA plan launch (too many for each CTA's shared memory); empty
+    sequences and a long one among them."""
+    rng = np.random.default_rng(41)
+    lens = rng.integers(0, 40, size=9000)
+    lens[4500] = 5000
+    out, ref = _random_decode(cuda_device, B=9000, H=1, D=64, bs=16, dtype=torch.float32, lmin=0, lmax=0, seed=41,
+                              lens=lens.tolist())
+    _check(out, ref, torch.float32)
+    assert b2pa.read_status(cuda_device) == 0
+
+
 def test_decode_long_contexts_split(cuda_device):
     # few sequences, long contexts: many pages per sequence -> split-K + combine
     out, ref = _random_decode(cuda_device, B=3, H=8, D=128, bs=16, dtype=torch.bfloat16, lmin=4000, lmax=9000,
