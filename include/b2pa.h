@@ -115,7 +115,11 @@ B2PA_API int b2pa_kv_append(const void* k_new, const int64_t new_k_strides[4],
  * Workspace bytes b2pa_paged_decode needs for this problem size.  Replaces
  * nothing in the reference (the Triton decode kernel runs one program per
  * (seq, head) with no split, triton_paged_attention.py:189); the split-K
- * partials of this backend live here.
+ * partials of this backend live here.  With at least 3 head-group streams
+ * (B * H / heads per group) per SM of the current device, the size depends on
+ * that device's SM count, not on max_pages: query it with the device current
+ * that will run the call (a call given less is refused with
+ * B2PA_ERR_WORKSPACE).
  */
 B2PA_API size_t b2pa_paged_decode_workspace_size(int B, int H, int D, int max_pages,
                                         int block_size, int dtype);
