@@ -127,6 +127,19 @@ def test_decode_contiguous_split_plan_kernel(cuda_device):
     assert b2pa.read_status(cuda_device) == 0
 
 
+def test_decode_contiguous_split_many_pieces(cuda_device):
+    """A 20,000-token sequence among 511 short ones (1,024 head-group
+    streams): with about 8 pages per CTA its streams are cut into well over
+    32 pieces, which the combine kernel merges 32 at a time."""
+    rng = np.random.default_rng(43)
+    lens = rng.integers(0, 30, size=512)
+    lens[200] = 20000
+    out, ref = _random_decode(cuda_device, B=512, H=8, D=64, bs=16, dtype=torch.float32, lmin=0, lmax=0, seed=43,
+                              lens=lens.tolist())
+    _check(out, ref, torch.float32)
+    assert b2pa.read_status(cuda_device) == 0
+
+
 def test_decode_long_contexts_split(cuda_device):
     # few sequences, long contexts: many pages per sequence -> split-K + combine
     out, ref = _random_decode(cuda_device, B=3, H=8, D=128, bs=16, dtype=torch.bfloat16, lmin=4000, lmax=9000,
