@@ -94,21 +94,23 @@ def _many_stream_lengths(rng, B):
     return lens.tolist()
 
 
-@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 16), (torch.float32, 32)])
-def test_decode_contiguous_split(cuda_device, dtype, D):
-    """2400 head-group streams: each CTA streams an equal range of pages and
-    streams cut between CTAs are merged by the combine kernel; cur_len 0 / 2 /
-    past the length included.  Two calls give the same bytes."""
+@pytest.mark.parametrize("dtype,D,bs", [(torch.bfloat16, 16, 16), (torch.float32, 32, 16), (torch.float16, 128, 16),
+                                        (torch.bfloat16, 64, 8), (torch.float32, 64, 32)])
+def test_decode_contiguous_split(cuda_device, dtype, D, bs):
+    """2400 or more head-group streams: each CTA streams an equal range of
+    pages and streams cut between CTAs are merged by the combine kernel;
+    cur_len 0 / 2 / past the length included.  Two calls give the same
+    bytes."""
     rng = np.random.default_rng(31)
     B, H = 1200, 8
     lens = _many_stream_lengths(rng, B)
     cur = [1] * B
     cur[3], cur[9], cur[700], cur[11] = 0, 2, 3, 500
-    out, ref = _random_decode(cuda_device, B=B, H=H, D=D, bs=16, dtype=dtype, lmin=0, lmax=0, seed=31, cur=cur,
+    out, ref = _random_decode(cuda_device, B=B, H=H, D=D, bs=bs, dtype=dtype, lmin=0, lmax=0, seed=31, cur=cur,
                               lens=lens)
     _check(out, ref, dtype)
     assert out[6].abs().sum().item() == 0 and out[11].abs().sum().item() == 0
-    again, _ = _random_decode(cuda_device, B=B, H=H, D=D, bs=16, dtype=dtype, lmin=0, lmax=0, seed=31, cur=cur,
+    again, _ = _random_decode(cuda_device, B=B, H=H, D=D, bs=bs, dtype=dtype, lmin=0, lmax=0, seed=31, cur=cur,
                               lens=lens)
     assert torch.equal(out, again)
     assert b2pa.read_status(cuda_device) == 0
